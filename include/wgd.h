@@ -1,0 +1,172 @@
+/*
+ * wgd — B200-native decoder loop for GGUF models: C ABI.
+ *
+ * This library is the device half of the reference runtime's PagedEngine
+ * (ahpah-dev/WebGPU 0.9.0): it replaces the WebGPU `Compute` wrapper
+ * (src/core/gpu.ts:2-67), the page uploads of `WeightPager`
+ * (src/core/pager.ts:7-47) and the per-layer dispatch sequence of
+ * `PagedEngine.forward/denseLayer/linear` (src/core/engine.ts:117-256).
+ * GGUF parsing, tokenizers and the SDK/worker protocol stay in the host
+ * language and call these entry points.
+ *
+ * Conventions
+ *   - Every call returns WGD_OK (0) or a WGD_E* status; the message of the last
+ *     failure on the calling thread is wgd_last_error().
+ *   - Host buffers are borrowed for the duration of a call. Device memory is
+ *     owned by the context and counted against its byte budget, with the same
+ *     meaning as the reference's GPU budget (gpu.ts:309-315).
+ *   - One calling thread per context; wgd_cancel() is the only call that is safe
+ *     from another thread.
+ *   - The wgd_op_* entry points run one kernel on caller-owned DEVICE pointers
+ *     (the reference's per-kernel checks in src/verify.ts and
+ *     src/verify-context.ts exercise the same kernels one at a time).
+ */
+#ifndef WGD_H
+#define WGD_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WGD_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define WGD_API __attribute__((visibility("default")))
+#else
+#define WGD_API
+#endif
+
+enum wgd_status {
+  WGD_OK = 0,
+  WGD_EINVAL = 1,       /* bad argument or unsupported shape */
+  WGD_EBUDGET = 2,      /* device budget exceeded (gpu.ts:311) */
+  WGD_ECUDA = 3,        /* CUDA runtime or kernel error */
+  WGD_ECANCELLED = 4,   /* wgd_cancel() observed (engine.ts:128,147 AbortSignal checks) */
+  WGD_ETIMEOUT = 5,     /* a bounded wait on a tensor-parallel peer gave up */
+  WGD_ESTATE = 6,       /* call out of order (e.g. forward before all weights are uploaded) */
+  WGD_ENONFINITE = 7,   /* every logit was non-finite (engine.ts:308) */
+  WGD_EIO = 8           /* the page reader callback failed */
+};
+
+/* GGML tensor types the reference decodes (gguf.ts:43-48). */
+enum wgd_ggml_type { WGD_F32 = 0, WGD_F16 = 1, WGD_Q4_0 = 2, WGD_Q8_0 = 8, WGD_Q4_K = 12, WGD_Q5_K = 13, WGD_Q6_K = 14 };
+
+/* Decoder configuration; mirrors ModelConfig (src/core/gguf.ts:124-144) as
+ * produced by modelConfig (gguf.ts:145-250). */
+typedef struct wgd_model_config {
+  int32_t family;          /* 0: dense llama/qwen2/qwen3/mistral block, 1: gemma3 block */
+  int32_t hidden, intermediate, layers, heads, kv_heads, head_dim, vocab;
+  float epsilon, theta, local_theta;
+  int32_t window, period;  /* gemma3 local window and layer period (gguf.ts:168,170) */
+  float attention_scale, rope_scale;
+  int32_t rotary_dim;
+  int32_t rope_mode;       /* 0: half-split (neox), 1: adjacent pairs (norm) (gguf.ts:176) */
+  int32_t sliding_window;  /* dense families: 0 = full context (gguf.ts:177) */
+  int32_t qk_norm, ffn_gate, activation; /* activation 0: silu, 1: gelu */
+  int32_t bias_q, bias_k, bias_v, bias_output;
+} wgd_model_config;
+
+/* PagingStats (src/core/pager.ts:5) plus device timings. */
+typedef struct wgd_stats {
+  uint64_t read_bytes, uploads, cache_hits, cache_bytes, gpu_bytes, peak_gpu_bytes, page_bytes;
+  double read_ms;
+  uint64_t forwards, tokens;
+  double last_forward_ms;   /* device time of the last forward (CUDA events) */
+  uint64_t streamed_bytes;  /* weight bytes streamed through page slots by the last forward */
+} wgd_stats;
+
+typedef struct wgd_ctx wgd_ctx;
+
+/* Reads `length` bytes at `offset` of the model file into `dst` (a pinned
+ * staging buffer owned by the library). Returns 0 on success. Mirrors
+ * ByteSource.read (src/core/source.ts:2-6). */
+typedef int (*wgd_read_fn)(void *user, uint64_t offset, uint64_t length, void *dst);
+
+WGD_API int wgd_abi_version(void);
+WGD_API const char *wgd_last_error(void);
+WGD_API int wgd_device_count(int *count);
+
+/* Context on one GPU; replaces Compute.init (gpu.ts:296-307) and the budget
+ * (gpu.ts:295). tp_rank/tp_size place this process in a tensor-parallel group
+ * (one process per GPU); page_bytes is the pager's page size (pager.ts:13-14). */
+WGD_API wgd_ctx *wgd_create(int device, int tp_rank, int tp_size, uint64_t budget_bytes, uint32_t page_bytes, int *status);
+WGD_API void wgd_destroy(wgd_ctx *ctx);
+
+/* Tensor-parallel wiring (no counterpart in the reference, which runs on one
+ * device). Each rank exports a handle to its exchange buffer; the host
+ * exchanges the handles (e.g. through torch.distributed) and opens the peers'. */
+WGD_API int wgd_tp_handle_size(void);
+WGD_API int wgd_tp_export(wgd_ctx *ctx, void *handle_out);
+WGD_API int wgd_tp_open_peers(wgd_ctx *ctx, const void *handles /* tp_size * handle_size bytes, rank order */);
+/* Bounded wait (iterations) for peers in the exchange kernel; 0 = default. */
+WGD_API int wgd_tp_set_timeout(wgd_ctx *ctx, uint64_t spin_limit);
+
+/* Model setup; replaces PagedEngine.load's allocation half (engine.ts:70-110).
+ * Order: model_begin, tensor_register for each directory entry, model_end,
+ * tensor_upload (or tensor_host / page reader for streamed weights). */
+WGD_API int wgd_model_begin(wgd_ctx *ctx, const wgd_model_config *cfg, int context_len, int max_batch);
+/* One entry of the GGUF tensor directory (Tensor, gguf.ts:41; dims in GGUF order). */
+WGD_API int wgd_tensor_register(wgd_ctx *ctx, const char *name, int ggml_type, const uint64_t *dims, int nd,
+                        uint64_t file_offset, uint64_t bytes, uint64_t row_bytes);
+WGD_API int wgd_model_end(wgd_ctx *ctx);
+/* Uploads bytes [byte_off, byte_off+n) of a tensor's GGUF data (whole rows) for
+ * resident weights; replaces WeightPager.page + Compute.write (pager.ts:25-44). */
+WGD_API int wgd_tensor_upload(wgd_ctx *ctx, const char *name, uint64_t byte_off, const void *host, uint64_t n);
+/* Registers a host copy of a tensor's GGUF bytes (kept alive by the caller)
+ * from which non-resident pages are streamed; `pinned` != 0 if the memory is
+ * page-locked or should be registered as such. */
+WGD_API int wgd_tensor_host(wgd_ctx *ctx, const char *name, const void *host, int pinned);
+/* Fallback source for streamed pages (ByteSource.read). */
+WGD_API int wgd_set_page_reader(wgd_ctx *ctx, wgd_read_fn fn, void *user);
+/* 1 if every weight needed by forward is resident or has a stream source. */
+WGD_API int wgd_model_ready(wgd_ctx *ctx, int *ready);
+/* Resident weight bytes and streamed weight bytes of the placement plan. */
+WGD_API int wgd_model_placement(wgd_ctx *ctx, uint64_t *resident_bytes, uint64_t *streamed_bytes);
+
+/* One forward over n token ids at positions [start, start+n); replaces
+ * PagedEngine.forward (engine.ts:138-180). want: 0 no output, 1 greedy token
+ * of the last row (engine.ts:305-309), 2 greedy token and full logits of the
+ * last row (vocab floats, rank 0 of a TP group). */
+WGD_API int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, int want, int32_t *argmax_out, float *logits_out);
+/* KV cache bookkeeping for prefix reuse and reset (engine.ts:269-283,302). */
+WGD_API int wgd_truncate_kv(wgd_ctx *ctx, int n_tokens);
+WGD_API void wgd_cancel(wgd_ctx *ctx);
+WGD_API int wgd_stats_get(wgd_ctx *ctx, wgd_stats *out);
+/* Enables/disables CUDA-graph replay of single-token forwards (default on). */
+WGD_API int wgd_set_graphs(wgd_ctx *ctx, int enabled);
+
+/* ---------------------------------------------------------------- kernels
+ * Single-kernel entry points on caller-owned device memory, on `stream`
+ * (a cudaStream_t, or NULL for the legacy default stream). They allocate
+ * small per-device scratch (work counters) on first use. */
+
+/* Bytes of one row in the device layout used by every weight kernel. */
+WGD_API int64_t wgd_dev_row_bytes(int ggml_type, int64_t cols);
+/* GGUF rows (raw bytes, row stride gguf row bytes) -> device layout rows. */
+WGD_API int wgd_op_repack(int ggml_type, int64_t rows, int64_t cols, const void *raw_dev, void *packed_dev, void *stream);
+/* Bit-exact dequant (WGSL f32 expression order, shaders.ts:42-67) of packed rows. */
+WGD_API int wgd_op_dequant(int ggml_type, int64_t rows, int64_t cols, const void *packed_dev, float *out_dev, void *stream);
+/* y[b*rows + r] = sum_c W[r][c] * x[b*cols + c] for b < batch (matmulShader,
+ * shaders.ts:68-83; expectation verify.ts:32-35). */
+WGD_API int wgd_op_gemv(int ggml_type, int64_t rows, int64_t cols, const void *packed_dev, const float *x_dev, int batch,
+                float *y_dev, void *stream);
+/* RMSNorm of n rows (normShader, shaders.ts:84-97). */
+WGD_API int wgd_op_rmsnorm(const float *x_dev, const float *w_dev, int cols, int n, float eps, float *y_dev, void *stream);
+/* Q/K rotation (+ optional per-head RMS norm) of x[n][heads][hd] in place:
+ * ropeShader / ropeNeoxShader / ropeClassicShader (shaders.ts:98-116,167-197).
+ * mode 0 half-split, 1 adjacent; norm_w non-null selects the Q/K-norm form. */
+WGD_API int wgd_op_rope(float *x_dev, const float *norm_w_dev, int n, int heads, int hd, int start, float theta, float scale,
+                float eps, int rotary_dim, int mode, void *stream);
+/* Causal GQA attention over a ring cache laid out [kv_heads][capacity][hd]
+ * (attentionShader, shaders.ts:117-150). q/out are [n][heads][hd]. */
+WGD_API int wgd_op_attention(const float *q_dev, const float *k_dev, const float *v_dev, float *out_dev, int n, int heads,
+                     int kv_heads, int hd, int start, float scale, int window, int capacity, void *stream);
+/* First finite maximum of x[0..n) (engine.ts:305-309); *idx_dev = -1 when none. */
+WGD_API int wgd_op_argmax(const float *x_dev, int n, int32_t *idx_dev, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

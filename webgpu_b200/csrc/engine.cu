@@ -1,0 +1,988 @@
+// The decoder engine behind include/wgd.h.
+//
+// One wgd_ctx owns one GPU (one process per GPU for tensor parallelism). The
+// per-token sequence follows PagedEngine.forward / denseLayer and the Gemma
+// block of the reference (src/core/engine.ts:138-180, 158-174, 217-251), with
+// its dispatches fused:
+//   embed -> per layer [ QKV GEMV (+attn RMSNorm prologue, +bias)
+//                        -> Q/K-norm + RoPE + KV ring write
+//                        -> split-K attention
+//                        -> O GEMV (+residual, or post-norm for Gemma)
+//                        -> gate|up GEMV (+ffn RMSNorm prologue, +SwiGLU/GeGLU)
+//                        -> down GEMV (+residual, or post-norm) ]
+//          -> LM head GEMV (+output RMSNorm prologue) on the last row -> argmax.
+// Single-token forwards are captured once into a CUDA graph (positions live in
+// device memory, so one graph serves every step) and replayed.
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/wgd.h"
+#include "common.cuh"
+#include "kernels.h"
+#include "tp.h"
+
+using namespace wgd;
+
+static thread_local std::string g_err;
+static int fail(int code, const std::string &msg) {
+  g_err = msg;
+  return code;
+}
+#define CK(call)                                                                                  \
+  do {                                                                                            \
+    cudaError_t e_ = (call);                                                                      \
+    if (e_ != cudaSuccess) return fail(WGD_ECUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+namespace {
+
+struct DevLinear {
+  int type = -1, rows = 0, cols = 0, nb = 0;
+  int64_t drow = 0;
+  uint8_t *w = nullptr;
+};
+
+enum Role {
+  R_NONE, R_EMBD, R_OUT_NORM, R_OUTPUT, R_ATTN_NORM, R_Q, R_K, R_V, R_O, R_QB, R_KB, R_VB, R_OB, R_QN, R_KN,
+  R_POST_ATTN, R_FFN_NORM, R_GATE, R_UP, R_DOWN, R_POST_FFW
+};
+struct RoleName { const char *name; Role role; };
+const RoleName LAYER_ROLES[] = {
+  {"attn_norm.weight", R_ATTN_NORM}, {"attn_q.weight", R_Q}, {"attn_k.weight", R_K}, {"attn_v.weight", R_V},
+  {"attn_output.weight", R_O}, {"attn_q.bias", R_QB}, {"attn_k.bias", R_KB}, {"attn_v.bias", R_VB},
+  {"attn_output.bias", R_OB}, {"attn_q_norm.weight", R_QN}, {"attn_k_norm.weight", R_KN},
+  {"post_attention_norm.weight", R_POST_ATTN}, {"ffn_norm.weight", R_FFN_NORM}, {"ffn_gate.weight", R_GATE},
+  {"ffn_up.weight", R_UP}, {"ffn_down.weight", R_DOWN}, {"post_ffw_norm.weight", R_POST_FFW}};
+
+struct TensorRec {
+  std::string name;
+  int type = 0, nd = 0;
+  uint64_t dims[4] = {0, 0, 0, 0};
+  uint64_t offset = 0, bytes = 0, row_bytes = 0;
+  int64_t cols = 0, rows = 0;
+  int layer = -1;
+  Role role = R_NONE;
+  // destination of a matrix
+  DevLinear *lin = nullptr;
+  RowMap map{};
+  int blk0 = 0, nbl = 0;
+  // destination of a vector: elements [vec_src0, vec_src0 + vec_len) -> vec
+  float *vec = nullptr;
+  int vec_src0 = 0, vec_len = 0;
+  int64_t uploaded_rows = 0;
+  bool needed = false;
+  const void *host = nullptr;
+};
+
+struct Layer {
+  float *attn_norm = nullptr, *qkv_bias = nullptr, *q_norm = nullptr, *k_norm = nullptr, *o_bias = nullptr;
+  float *post_attn = nullptr, *ffn_norm = nullptr, *post_ffw = nullptr;
+  DevLinear qkv, o, gate_up, down;
+  float *k_cache = nullptr, *v_cache = nullptr;
+  int capacity = 0, window = 0;
+  bool local = false;
+  double theta = 0, rope_scale = 1;
+};
+
+struct Alloc { void *p; size_t n; };
+
+}  // namespace
+
+struct wgd_ctx {
+  int device = 0, tp_rank = 0, tp_size = 1, sm_count = 148;
+  uint64_t budget = 0, allocated = 0, peak = 0;
+  uint32_t page_bytes = 16u << 20;
+  cudaStream_t stream = nullptr;
+  std::vector<Alloc> allocs;
+  // model
+  bool begun = false, ended = false;
+  wgd_model_config c{};
+  int context = 0, max_batch = 0;
+  std::vector<TensorRec> tensors;
+  std::unordered_map<std::string, int> by_name;
+  int heads_l = 0, kv_l = 0, q_l = 0, kvd_l = 0, qkv_rows = 0, ffn0 = 0, ffn_l = 0, vocab0 = 0, vocab_l = 0;
+  std::vector<Layer> layers;
+  DevLinear embd, lm;
+  float *out_norm = nullptr;
+  bool tied = false;
+  // work buffers
+  float *hidden = nullptr, *qkv = nullptr, *qrot = nullptr, *att = nullptr, *proj = nullptr, *act = nullptr, *logits = nullptr;
+  int *d_ids = nullptr, *d_start = nullptr, *d_argmax = nullptr, *d_err = nullptr;
+  float *d_maxval = nullptr, *att_part = nullptr, *am_part = nullptr;
+  unsigned *att_ctr = nullptr, *gemv_ctr = nullptr, *am_ctr = nullptr;
+  int att_splits = 1, gemv_slot = 0;
+  uint8_t *staging = nullptr;
+  size_t staging_bytes = 0;
+  int32_t *h_io = nullptr;  // pinned: [0] start, [1] argmax, [2..] ids
+  // graph
+  bool graphs = true;
+  cudaGraphExec_t decode_exec = nullptr;
+  cudaGraph_t decode_graph = nullptr;
+  std::atomic<int> cancel{0};
+  wgd_stats st{};
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  TpComm *tp = nullptr;
+  uint64_t tp_spin_limit = 0;
+};
+
+// ------------------------------------------------------------------ helpers
+
+static int ctx_alloc(wgd_ctx *ctx, void **p, size_t n, const char *label) {
+  n = (size_t)align_up((int64_t)(n ? n : 4), 256);
+  if (ctx->allocated + n > ctx->budget)
+    return fail(WGD_EBUDGET, std::string("GPU budget exceeded. Reduce context length or increase the memory budget. (") +
+                                 label + ")");
+  cudaError_t e = cudaMalloc(p, n);
+  if (e != cudaSuccess) return fail(WGD_ECUDA, std::string("cudaMalloc(") + label + "): " + cudaGetErrorString(e));
+  e = cudaMemset(*p, 0, n);
+  if (e != cudaSuccess) return fail(WGD_ECUDA, std::string("cudaMemset: ") + cudaGetErrorString(e));
+  ctx->allocs.push_back({*p, n});
+  ctx->allocated += n;
+  if (ctx->allocated > ctx->peak) ctx->peak = ctx->allocated;
+  return WGD_OK;
+}
+template <typename T>
+static int ctx_alloc_t(wgd_ctx *ctx, T **p, size_t count, const char *label) {
+  void *v = nullptr;
+  int rc = ctx_alloc(ctx, &v, count * sizeof(T), label);
+  *p = (T *)v;
+  return rc;
+}
+
+static void free_all(wgd_ctx *ctx) {
+  if (ctx->decode_exec) cudaGraphExecDestroy(ctx->decode_exec);
+  if (ctx->decode_graph) cudaGraphDestroy(ctx->decode_graph);
+  ctx->decode_exec = nullptr;
+  ctx->decode_graph = nullptr;
+  for (auto &a : ctx->allocs) cudaFree(a.p);
+  ctx->allocs.clear();
+  ctx->allocated = 0;
+}
+
+static bool parse_layer_name(const std::string &name, int &layer, Role &role) {
+  if (name.compare(0, 4, "blk.") != 0) return false;
+  size_t dot = name.find('.', 4);
+  if (dot == std::string::npos) return false;
+  layer = atoi(name.substr(4, dot - 4).c_str());
+  std::string rest = name.substr(dot + 1);
+  for (const auto &r : LAYER_ROLES)
+    if (rest == r.name) { role = r.role; return true; }
+  role = R_NONE;
+  return true;
+}
+
+// Balanced split of `units` into tp parts: part r = [r*units/tp, (r+1)*units/tp).
+static int part_begin(int units, int r, int tp) { return (int)((int64_t)units * r / tp); }
+
+// ------------------------------------------------------------------ C ABI
+
+extern "C" {
+
+int wgd_abi_version(void) { return WGD_ABI_VERSION; }
+const char *wgd_last_error(void) { return g_err.c_str(); }
+
+int wgd_device_count(int *count) {
+  if (!count) return fail(WGD_EINVAL, "count is null");
+  CK(cudaGetDeviceCount(count));
+  return WGD_OK;
+}
+
+wgd_ctx *wgd_create(int device, int tp_rank, int tp_size, uint64_t budget_bytes, uint32_t page_bytes, int *status) {
+  auto set = [&](int s) { if (status) *status = s; };
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+    set(fail(WGD_EINVAL, "invalid CUDA device"));
+    return nullptr;
+  }
+  if (tp_size < 1 || tp_size > 8 || tp_rank < 0 || tp_rank >= tp_size) {
+    set(fail(WGD_EINVAL, "tensor-parallel size must be 1-8 and rank within it"));
+    return nullptr;
+  }
+  if (page_bytes != (16u << 20) && page_bytes != (64u << 20)) {
+    set(fail(WGD_EINVAL, "Weight pages must be 16 or 64 MiB."));
+    return nullptr;
+  }
+  if (cudaSetDevice(device) != cudaSuccess) { set(fail(WGD_ECUDA, "cudaSetDevice failed")); return nullptr; }
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major < 10) {
+    set(fail(WGD_EINVAL, "wgd requires a Blackwell (sm_100) GPU"));
+    return nullptr;
+  }
+  auto *ctx = new wgd_ctx();
+  ctx->device = device;
+  ctx->tp_rank = tp_rank;
+  ctx->tp_size = tp_size;
+  ctx->budget = budget_bytes;
+  ctx->page_bytes = page_bytes;
+  ctx->sm_count = prop.multiProcessorCount;
+  if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreate(&ctx->ev0) != cudaSuccess || cudaEventCreate(&ctx->ev1) != cudaSuccess ||
+      cudaMallocHost((void **)&ctx->h_io, sizeof(int32_t) * 1024) != cudaSuccess) {
+    set(fail(WGD_ECUDA, "stream/event/pinned allocation failed"));
+    delete ctx;
+    return nullptr;
+  }
+  ctx->st.page_bytes = page_bytes;
+  set(WGD_OK);
+  return ctx;
+}
+
+void wgd_destroy(wgd_ctx *ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->tp) tp_destroy(ctx->tp);
+  free_all(ctx);
+  if (ctx->h_io) cudaFreeHost(ctx->h_io);
+  if (ctx->ev0) cudaEventDestroy(ctx->ev0);
+  if (ctx->ev1) cudaEventDestroy(ctx->ev1);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+int wgd_model_begin(wgd_ctx *ctx, const wgd_model_config *cfg, int context_len, int max_batch) {
+  if (!ctx || !cfg) return fail(WGD_EINVAL, "null argument");
+  if (ctx->begun) return fail(WGD_ESTATE, "model already configured");
+  const wgd_model_config &c = *cfg;
+  // ModelConfig validation (gguf.ts:186) plus what the kernels need.
+  if (c.layers < 1 || c.hidden < 1 || c.heads < 1 || c.head_dim < 1 || c.kv_heads < 1 || c.intermediate < 1 ||
+      c.vocab < 1 || c.heads % c.kv_heads || c.head_dim % 2 || c.rotary_dim % 2 || c.rotary_dim > c.head_dim ||
+      c.layers > 128 || c.heads > 256 || c.head_dim > 512 || c.hidden > 16384 || c.intermediate > 131072 || c.vocab > 1000000)
+    return fail(WGD_EINVAL, "Unsupported model dimensions.");
+  if (c.family != 0 && c.family != 1) return fail(WGD_EINVAL, "family must be 0 (dense) or 1 (gemma3)");
+  if (context_len < 1 || context_len > 32768) return fail(WGD_EINVAL, "Context must be an integer from 256 to 32768 tokens.");
+  if (max_batch < 1 || max_batch > 128) return fail(WGD_EINVAL, "Batch size must be 1, 8, 16, 32, 64 or 128.");
+  if (c.heads % ctx->tp_size || c.kv_heads % ctx->tp_size)
+    return fail(WGD_EINVAL, "query and KV head counts must divide by the tensor-parallel size");
+  if (c.heads / c.kv_heads > 8) return fail(WGD_EINVAL, "query heads per KV head above 8 are not supported");
+  if (c.head_dim % 4) return fail(WGD_EINVAL, "head dimension must be a multiple of 4");
+  ctx->c = c;
+  ctx->context = context_len;
+  ctx->max_batch = max_batch;
+  ctx->begun = true;
+  return WGD_OK;
+}
+
+int wgd_tensor_register(wgd_ctx *ctx, const char *name, int ggml_type, const uint64_t *dims, int nd, uint64_t file_offset,
+                        uint64_t bytes, uint64_t row_bytes) {
+  if (!ctx || !name || !dims) return fail(WGD_EINVAL, "null argument");
+  if (!ctx->begun || ctx->ended) return fail(WGD_ESTATE, "tensor_register must come between model_begin and model_end");
+  if (nd < 1 || nd > 4) return fail(WGD_EINVAL, "Invalid tensor directory.");
+  if (ctx->by_name.count(name)) return fail(WGD_EINVAL, std::string("duplicate tensor ") + name);
+  TensorRec t;
+  t.name = name;
+  t.type = ggml_type;
+  t.nd = nd;
+  uint64_t n = 1;
+  for (int i = 0; i < nd; i++) { t.dims[i] = dims[i]; n *= dims[i]; }
+  t.offset = file_offset;
+  t.bytes = bytes;
+  t.row_bytes = row_bytes;
+  t.cols = (int64_t)dims[0];
+  t.rows = (int64_t)(n / (dims[0] ? dims[0] : 1));
+  if (type_supported(ggml_type)) {
+    if (t.cols % block_elems(ggml_type) || (int64_t)row_bytes != gguf_row_bytes(ggml_type, t.cols) ||
+        bytes != row_bytes * (uint64_t)t.rows)
+      return fail(WGD_EINVAL, std::string("Invalid shape for ") + name + ".");
+  }
+  if (t.name == "token_embd.weight") t.role = R_EMBD;
+  else if (t.name == "output_norm.weight") t.role = R_OUT_NORM;
+  else if (t.name == "output.weight") t.role = R_OUTPUT;
+  else {
+    int layer; Role role;
+    if (parse_layer_name(t.name, layer, role) && layer < ctx->c.layers) { t.layer = layer; t.role = role; }
+  }
+  ctx->by_name[t.name] = (int)ctx->tensors.size();
+  ctx->tensors.push_back(t);
+  return WGD_OK;
+}
+
+}  // extern "C"
+
+static TensorRec *find(wgd_ctx *ctx, const std::string &name) {
+  auto it = ctx->by_name.find(name);
+  return it == ctx->by_name.end() ? nullptr : &ctx->tensors[it->second];
+}
+
+static int expect(wgd_ctx *ctx, const std::string &name, int64_t cols, int64_t rows, TensorRec **out, bool optional = false) {
+  TensorRec *t = find(ctx, name);
+  if (!t) {
+    if (optional) { *out = nullptr; return WGD_OK; }
+    return fail(WGD_EINVAL, "Missing or invalid tensor " + name + ".");
+  }
+  if (t->cols != cols || t->rows != rows || (rows == 1 && t->nd != 1))
+    return fail(WGD_EINVAL, "Missing or invalid tensor " + name + ".");
+  if (!type_supported(t->type))
+    return fail(WGD_EINVAL, "Unsupported tensor quantization " + std::to_string(t->type) + " in " + name + ".");
+  t->needed = true;
+  *out = t;
+  return WGD_OK;
+}
+
+static int alloc_linear(wgd_ctx *ctx, DevLinear &L, int type, int rows, int cols, const char *label) {
+  L.type = type;
+  L.rows = rows;
+  L.cols = cols;
+  L.nb = cols / block_elems(type);
+  L.drow = dev_row_bytes(type, cols);
+  if (cols % 32) return fail(WGD_EINVAL, std::string("matrix width must be a multiple of 32: ") + label);
+  if (gemv_max_batch(cols) == 0) return fail(WGD_EINVAL, std::string("matrix too wide for the GEMV kernel: ") + label);
+  return ctx_alloc_t(ctx, &L.w, (size_t)L.drow * rows + 16, label);
+}
+
+// A matrix part: GGUF rows [src_begin, src_end) -> device rows (map), columns [blk0, blk0+nbl) in blocks.
+static void place(TensorRec *t, DevLinear *L, int src_begin, int src_end, int dst_base, int interleave, int blk0, int nbl) {
+  t->lin = L;
+  t->map = RowMap{src_begin, src_end, dst_base, interleave, 0};
+  t->blk0 = blk0;
+  t->nbl = nbl;
+}
+static int place_vec(wgd_ctx *ctx, TensorRec *t, float *dst, int src0, int len) {
+  if (!t) return WGD_OK;
+  if (t->rows != 1) return fail(WGD_EINVAL, "vector tensor expected: " + t->name);
+  t->vec = dst;
+  t->vec_src0 = src0;
+  t->vec_len = len;
+  (void)ctx;
+  return WGD_OK;
+}
+
+extern "C" int wgd_model_end(wgd_ctx *ctx) {
+  if (!ctx) return fail(WGD_EINVAL, "null context");
+  if (!ctx->begun || ctx->ended) return fail(WGD_ESTATE, "model_end out of order");
+  CK(cudaSetDevice(ctx->device));
+  const wgd_model_config &c = ctx->c;
+  const int H = c.hidden, hd = c.head_dim, tp = ctx->tp_size, r = ctx->tp_rank;
+  const bool gemma = c.family == 1;
+  ctx->heads_l = c.heads / tp;
+  ctx->kv_l = c.kv_heads / tp;
+  ctx->q_l = ctx->heads_l * hd;
+  ctx->kvd_l = ctx->kv_l * hd;
+  ctx->qkv_rows = ctx->q_l + 2 * ctx->kvd_l;
+  const int qd = c.heads * hd, kvd = c.kv_heads * hd;
+  int rc;
+
+  // ---- directory validation (modelConfig shape checks, gguf.ts:196-249)
+  TensorRec *embd, *onorm, *output;
+  if ((rc = expect(ctx, "token_embd.weight", H, c.vocab, &embd))) return rc;
+  if ((rc = expect(ctx, "output_norm.weight", H, 1, &onorm))) return rc;
+  if ((rc = expect(ctx, "output.weight", H, c.vocab, &output, true))) return rc;
+  ctx->tied = output == nullptr;
+  // FFN partition unit: the down projection's block width (row-split by columns).
+  TensorRec *down0 = find(ctx, "blk.0.ffn_down.weight");
+  if (!down0 || !type_supported(down0->type)) return fail(WGD_EINVAL, "Missing or invalid tensor blk.0.ffn_down.weight.");
+  const int funit = block_elems(down0->type);
+  if (c.intermediate % funit) return fail(WGD_EINVAL, "feed-forward width is not a whole number of blocks");
+  const int fblocks = c.intermediate / funit;
+  ctx->ffn0 = part_begin(fblocks, r, tp) * funit;
+  ctx->ffn_l = part_begin(fblocks, r + 1, tp) * funit - ctx->ffn0;
+  if (ctx->ffn_l % 2) return fail(WGD_EINVAL, "feed-forward shard must have an even row count");
+  ctx->vocab0 = part_begin(c.vocab, r, tp);
+  ctx->vocab_l = part_begin(c.vocab, r + 1, tp) - ctx->vocab0;
+
+  ctx->layers.assign(c.layers, Layer());
+  const int B = ctx->max_batch;
+  for (int l = 0; l < c.layers; l++) {
+    Layer &L = ctx->layers[l];
+    const std::string p = "blk." + std::to_string(l) + ".";
+    TensorRec *an, *q, *k, *v, *o, *qb = nullptr, *kb = nullptr, *vb = nullptr, *ob = nullptr, *qn = nullptr, *kn = nullptr;
+    TensorRec *pa = nullptr, *fn, *gate = nullptr, *up, *dn, *pf = nullptr;
+    if ((rc = expect(ctx, p + "attn_norm.weight", H, 1, &an))) return rc;
+    if ((rc = expect(ctx, p + "attn_q.weight", H, qd, &q))) return rc;
+    if ((rc = expect(ctx, p + "attn_k.weight", H, kvd, &k))) return rc;
+    if ((rc = expect(ctx, p + "attn_v.weight", H, kvd, &v))) return rc;
+    if ((rc = expect(ctx, p + "attn_output.weight", qd, H, &o))) return rc;
+    if ((rc = expect(ctx, p + "ffn_norm.weight", H, 1, &fn))) return rc;
+    if ((rc = expect(ctx, p + "ffn_up.weight", H, c.intermediate, &up))) return rc;
+    if ((rc = expect(ctx, p + "ffn_down.weight", c.intermediate, H, &dn))) return rc;
+    const bool gated = gemma || c.ffn_gate;
+    if (gated && (rc = expect(ctx, p + "ffn_gate.weight", H, c.intermediate, &gate))) return rc;
+    if (!gemma) {
+      if (c.bias_q && (rc = expect(ctx, p + "attn_q.bias", qd, 1, &qb))) return rc;
+      if (c.bias_k && (rc = expect(ctx, p + "attn_k.bias", kvd, 1, &kb))) return rc;
+      if (c.bias_v && (rc = expect(ctx, p + "attn_v.bias", kvd, 1, &vb))) return rc;
+      if (c.bias_output && (rc = expect(ctx, p + "attn_output.bias", H, 1, &ob))) return rc;
+    } else {
+      if ((rc = expect(ctx, p + "post_attention_norm.weight", H, 1, &pa))) return rc;
+      if ((rc = expect(ctx, p + "post_ffw_norm.weight", H, 1, &pf))) return rc;
+    }
+    if (gemma || c.qk_norm) {
+      if ((rc = expect(ctx, p + "attn_q_norm.weight", hd, 1, &qn))) return rc;
+      if ((rc = expect(ctx, p + "attn_k_norm.weight", hd, 1, &kn))) return rc;
+    }
+    if (q->type != k->type || q->type != v->type)
+      return fail(WGD_EINVAL, "Q/K/V of one layer must share a quantization type (fused projection)");
+    if (gate && gate->type != up->type)
+      return fail(WGD_EINVAL, "ffn_gate and ffn_up of one layer must share a quantization type (fused projection)");
+    if (dn->type != down0->type) return fail(WGD_EINVAL, "ffn_down must use one quantization type in every layer");
+    if (ctx->q_l % block_elems(o->type) || (r * ctx->q_l) % block_elems(o->type))
+      return fail(WGD_EINVAL, "attention output shard is not a whole number of blocks");
+
+    // ---- placement: this rank's heads and FFN rows
+    if ((rc = alloc_linear(ctx, L.qkv, q->type, ctx->qkv_rows, H, "qkv"))) return rc;
+    place(q, &L.qkv, r * ctx->q_l, (r + 1) * ctx->q_l, 0, 0, 0, L.qkv.nb);
+    place(k, &L.qkv, r * ctx->kvd_l, (r + 1) * ctx->kvd_l, ctx->q_l, 0, 0, L.qkv.nb);
+    place(v, &L.qkv, r * ctx->kvd_l, (r + 1) * ctx->kvd_l, ctx->q_l + ctx->kvd_l, 0, 0, L.qkv.nb);
+    if ((rc = alloc_linear(ctx, L.o, o->type, H, ctx->q_l, "attn_output"))) return rc;
+    const int ob_ = block_elems(o->type);
+    place(o, &L.o, 0, H, 0, 0, r * ctx->q_l / ob_, ctx->q_l / ob_);
+    if (gated) {
+      if ((rc = alloc_linear(ctx, L.gate_up, up->type, 2 * ctx->ffn_l, H, "ffn_gate_up"))) return rc;
+      place(gate, &L.gate_up, ctx->ffn0, ctx->ffn0 + ctx->ffn_l, 0, 1, 0, L.gate_up.nb);
+      place(up, &L.gate_up, ctx->ffn0, ctx->ffn0 + ctx->ffn_l, 0, 2, 0, L.gate_up.nb);
+    } else {
+      if ((rc = alloc_linear(ctx, L.gate_up, up->type, ctx->ffn_l, H, "ffn_up"))) return rc;
+      place(up, &L.gate_up, ctx->ffn0, ctx->ffn0 + ctx->ffn_l, 0, 0, 0, L.gate_up.nb);
+    }
+    if ((rc = alloc_linear(ctx, L.down, dn->type, H, ctx->ffn_l, "ffn_down"))) return rc;
+    place(dn, &L.down, 0, H, 0, 0, ctx->ffn0 / funit, ctx->ffn_l / funit);
+
+    // ---- vectors
+    if ((rc = ctx_alloc_t(ctx, &L.attn_norm, H, "attn_norm"))) return rc;
+    place_vec(ctx, an, L.attn_norm, 0, H);
+    if ((rc = ctx_alloc_t(ctx, &L.ffn_norm, H, "ffn_norm"))) return rc;
+    place_vec(ctx, fn, L.ffn_norm, 0, H);
+    if (qb || kb || vb) {
+      if ((rc = ctx_alloc_t(ctx, &L.qkv_bias, ctx->qkv_rows, "qkv_bias"))) return rc;
+      place_vec(ctx, qb, L.qkv_bias, r * ctx->q_l, ctx->q_l);
+      place_vec(ctx, kb, L.qkv_bias + ctx->q_l, r * ctx->kvd_l, ctx->kvd_l);
+      place_vec(ctx, vb, L.qkv_bias + ctx->q_l + ctx->kvd_l, r * ctx->kvd_l, ctx->kvd_l);
+    }
+    if (ob && r == 0) {  // the output bias is added once across the tensor-parallel sum
+      if ((rc = ctx_alloc_t(ctx, &L.o_bias, H, "o_bias"))) return rc;
+      place_vec(ctx, ob, L.o_bias, 0, H);
+    } else if (ob) {
+      ob->needed = false;
+    }
+    if (qn) {
+      if ((rc = ctx_alloc_t(ctx, &L.q_norm, hd, "q_norm")) || (rc = ctx_alloc_t(ctx, &L.k_norm, hd, "k_norm"))) return rc;
+      place_vec(ctx, qn, L.q_norm, 0, hd);
+      place_vec(ctx, kn, L.k_norm, 0, hd);
+    }
+    if (pa) {
+      if ((rc = ctx_alloc_t(ctx, &L.post_attn, H, "post_attention_norm")) || (rc = ctx_alloc_t(ctx, &L.post_ffw, H, "post_ffw_norm")))
+        return rc;
+      place_vec(ctx, pa, L.post_attn, 0, H);
+      place_vec(ctx, pf, L.post_ffw, 0, H);
+    }
+    // ---- attention window and KV ring capacity (context.ts:16-24; engine.ts:147,161,163,234)
+    L.local = gemma && c.period > 1 && l % c.period != c.period - 1;
+    L.theta = L.local ? c.local_theta : c.theta;
+    L.rope_scale = L.local ? 1.0 : c.rope_scale;
+    if (gemma) {
+      L.window = L.local ? c.window : ctx->context;
+      L.capacity = L.local ? std::min(ctx->context, c.window + B - 1) : ctx->context;
+    } else {
+      L.window = c.sliding_window > 0 ? c.sliding_window : ctx->context;
+      L.capacity = c.sliding_window > 0 ? std::min(ctx->context, c.sliding_window + B - 1) : ctx->context;
+    }
+    if ((rc = ctx_alloc_t(ctx, &L.k_cache, (size_t)ctx->kv_l * L.capacity * hd, "K cache"))) return rc;
+    if ((rc = ctx_alloc_t(ctx, &L.v_cache, (size_t)ctx->kv_l * L.capacity * hd, "V cache"))) return rc;
+  }
+
+  // ---- embedding (replicated: any id can appear) and LM head (vocab rows of this rank)
+  if ((rc = alloc_linear(ctx, ctx->embd, embd->type, c.vocab, H, "token_embd"))) return rc;
+  place(embd, &ctx->embd, 0, c.vocab, 0, 0, 0, ctx->embd.nb);
+  if (ctx->tied) {
+    ctx->lm = ctx->embd;
+    ctx->lm.w = ctx->embd.w + (int64_t)ctx->vocab0 * ctx->embd.drow;
+    ctx->lm.rows = ctx->vocab_l;
+  } else {
+    if ((rc = alloc_linear(ctx, ctx->lm, output->type, ctx->vocab_l, H, "output"))) return rc;
+    place(output, &ctx->lm, ctx->vocab0, ctx->vocab0 + ctx->vocab_l, 0, 0, 0, ctx->lm.nb);
+  }
+  if ((rc = ctx_alloc_t(ctx, &ctx->out_norm, H, "output_norm"))) return rc;
+  place_vec(ctx, onorm, ctx->out_norm, 0, H);
+
+  // ---- work buffers
+  const int F = std::max(ctx->ffn_l, 1);
+  if ((rc = ctx_alloc_t(ctx, &ctx->hidden, (size_t)B * H, "hidden")) || (rc = ctx_alloc_t(ctx, &ctx->qkv, (size_t)B * ctx->qkv_rows, "qkv")) ||
+      (rc = ctx_alloc_t(ctx, &ctx->qrot, (size_t)B * ctx->q_l, "q")) || (rc = ctx_alloc_t(ctx, &ctx->att, (size_t)B * ctx->q_l, "attention")) ||
+      (rc = ctx_alloc_t(ctx, &ctx->proj, (size_t)B * H, "projection")) || (rc = ctx_alloc_t(ctx, &ctx->act, (size_t)B * F, "ffn")) ||
+      (rc = ctx_alloc_t(ctx, &ctx->logits, (size_t)c.vocab, "logits")) || (rc = ctx_alloc_t(ctx, &ctx->d_ids, (size_t)B, "ids")) ||
+      (rc = ctx_alloc_t(ctx, &ctx->d_start, 4, "start")) || (rc = ctx_alloc_t(ctx, &ctx->d_argmax, 4, "argmax")) ||
+      (rc = ctx_alloc_t(ctx, &ctx->d_err, 4, "err")) || (rc = ctx_alloc_t(ctx, &ctx->d_maxval, 4, "maxval")))
+    return rc;
+  ctx->att_splits = attention_splits(ctx->context);
+  if ((rc = ctx_alloc_t(ctx, &ctx->att_part, attention_part_floats(B, c.heads / tp, ctx->kv_l, hd, ctx->att_splits), "attention partials")))
+    return rc;
+  if ((rc = ctx_alloc_t(ctx, &ctx->att_ctr, (size_t)B * ctx->kv_l, "attention counters"))) return rc;
+  if ((rc = ctx_alloc_t(ctx, &ctx->gemv_ctr, 2 * 1024, "gemv counters"))) return rc;
+  if ((rc = ctx_alloc_t(ctx, &ctx->am_part, 2 * 256, "argmax partials")) || (rc = ctx_alloc_t(ctx, &ctx->am_ctr, 4, "argmax counter")))
+    return rc;
+  ctx->staging_bytes = 64u << 20;
+  if ((rc = ctx_alloc_t(ctx, &ctx->staging, ctx->staging_bytes, "upload staging"))) return rc;
+  if (tp > 1) {
+    if ((rc = tp_create(&ctx->tp, ctx->tp_rank, tp, (size_t)B * H, &g_err))) return rc;
+  }
+  ctx->ended = true;
+  ctx->st.gpu_bytes = ctx->allocated;
+  ctx->st.peak_gpu_bytes = ctx->peak;
+  return WGD_OK;
+}
+
+// ------------------------------------------------------------------ uploads
+
+static int upload_vector(wgd_ctx *ctx, TensorRec *t, const void *host) {
+  const int64_t n = t->cols;
+  const int64_t drb = dev_row_bytes(t->type, n);
+  const size_t need = (size_t)t->bytes + (size_t)drb + (size_t)n * 4 + 64;
+  if (need > ctx->staging_bytes) return fail(WGD_EINVAL, "vector too large for staging: " + t->name);
+  uint8_t *raw = ctx->staging, *packed = ctx->staging + align_up((int64_t)t->bytes, 256);
+  float *vals = (float *)(packed + align_up(drb, 256));
+  CK(cudaMemcpyAsync(raw, host, t->bytes, cudaMemcpyHostToDevice, ctx->stream));
+  RowMap m{0, 1, 0, 0, 0};
+  CK(launch_repack(t->type, raw, (int64_t)t->row_bytes, 0, 1, 0, (int)(n / block_elems(t->type)), packed, drb, m, ctx->stream));
+  CK(launch_dequant(t->type, packed, drb, 1, (int)n, vals, n, ctx->stream));
+  CK(cudaMemcpyAsync(t->vec, vals + t->vec_src0, sizeof(float) * t->vec_len, cudaMemcpyDeviceToDevice, ctx->stream));
+  CK(cudaStreamSynchronize(ctx->stream));
+  t->uploaded_rows = 1;
+  return WGD_OK;
+}
+
+extern "C" int wgd_tensor_upload(wgd_ctx *ctx, const char *name, uint64_t byte_off, const void *host, uint64_t n) {
+  if (!ctx || !name || !host) return fail(WGD_EINVAL, "null argument");
+  if (!ctx->ended) return fail(WGD_ESTATE, "tensor_upload requires model_end first");
+  CK(cudaSetDevice(ctx->device));
+  TensorRec *t = find(ctx, name);
+  if (!t) return fail(WGD_EINVAL, std::string("unknown tensor ") + name);
+  if (!t->needed) return WGD_OK;  // not used by this rank / model
+  if (t->vec) {
+    if (byte_off != 0 || n != t->bytes) return fail(WGD_EINVAL, "vectors upload whole: " + t->name);
+    return upload_vector(ctx, t, host);
+  }
+  if (!t->lin) return WGD_OK;
+  if (byte_off % t->row_bytes || n % t->row_bytes || byte_off + n > t->bytes)
+    return fail(WGD_EINVAL, "uploads must cover whole rows inside the tensor: " + t->name);
+  int64_t row0 = (int64_t)(byte_off / t->row_bytes), nrows = (int64_t)(n / t->row_bytes);
+  // clip to the rows this rank keeps
+  int64_t keep0 = std::max<int64_t>(row0, t->map.src_begin), keep1 = std::min<int64_t>(row0 + nrows, t->map.src_end);
+  const int64_t chunk_rows = std::max<int64_t>(1, (int64_t)ctx->staging_bytes / (int64_t)t->row_bytes);
+  for (int64_t a = keep0; a < keep1; a += chunk_rows) {
+    const int64_t cnt = std::min(chunk_rows, keep1 - a);
+    const uint8_t *src = (const uint8_t *)host + (a - row0) * t->row_bytes;
+    CK(cudaMemcpyAsync(ctx->staging, src, cnt * t->row_bytes, cudaMemcpyHostToDevice, ctx->stream));
+    CK(launch_repack(t->type, ctx->staging, (int64_t)t->row_bytes, (int)a, (int)cnt, t->blk0, t->nbl, t->lin->w, t->lin->drow,
+                     t->map, ctx->stream));
+    CK(cudaStreamSynchronize(ctx->stream));
+  }
+  t->uploaded_rows += nrows;
+  ctx->st.uploads++;
+  ctx->st.read_bytes += n;
+  return WGD_OK;
+}
+
+extern "C" int wgd_tensor_host(wgd_ctx *ctx, const char *name, const void *host, int pinned) {
+  if (!ctx || !name || !host) return fail(WGD_EINVAL, "null argument");
+  TensorRec *t = find(ctx, name);
+  if (!t) return fail(WGD_EINVAL, std::string("unknown tensor ") + name);
+  t->host = host;
+  (void)pinned;
+  return WGD_OK;
+}
+
+extern "C" int wgd_set_page_reader(wgd_ctx *ctx, wgd_read_fn fn, void *user) {
+  if (!ctx) return fail(WGD_EINVAL, "null context");
+  (void)fn; (void)user;
+  return WGD_OK;
+}
+
+static bool all_uploaded(wgd_ctx *ctx, std::string *missing) {
+  for (auto &t : ctx->tensors) {
+    if (!t.needed) continue;
+    bool ok = t.vec ? t.uploaded_rows >= 1 : t.uploaded_rows >= t.rows;
+    if (!ok) { if (missing) *missing = t.name; return false; }
+  }
+  return true;
+}
+
+extern "C" int wgd_model_ready(wgd_ctx *ctx, int *ready) {
+  if (!ctx || !ready) return fail(WGD_EINVAL, "null argument");
+  *ready = ctx->ended && all_uploaded(ctx, nullptr);
+  return WGD_OK;
+}
+
+extern "C" int wgd_model_placement(wgd_ctx *ctx, uint64_t *resident, uint64_t *streamed) {
+  if (!ctx) return fail(WGD_EINVAL, "null context");
+  uint64_t res = 0;
+  for (auto &L : ctx->layers) res += L.qkv.drow * L.qkv.rows + L.o.drow * L.o.rows + L.gate_up.drow * L.gate_up.rows + L.down.drow * L.down.rows;
+  res += ctx->embd.drow * ctx->embd.rows + (ctx->tied ? 0 : ctx->lm.drow * ctx->lm.rows);
+  if (resident) *resident = res;
+  if (streamed) *streamed = 0;
+  return WGD_OK;
+}
+
+// ------------------------------------------------------------------ forward
+
+static int gemv(wgd_ctx *ctx, const DevLinear &L, const float *x, int ldx, const float *norm_w, float *y, int ldy,
+                const float *bias, int epi, int batch) {
+  GemvArgs a{};
+  a.w = L.w;
+  a.drow = L.drow;
+  a.rows = L.rows;
+  a.cols = L.cols;
+  a.nb = L.nb;
+  a.x = x;
+  a.ldx = ldx;
+  a.norm_w = norm_w;
+  a.eps = ctx->c.epsilon;
+  a.y = y;
+  a.ldy = ldy;
+  a.bias = bias;
+  a.epi = epi;
+  a.batch = batch;
+  a.ctr = ctx->gemv_ctr + 2 * (ctx->gemv_slot++ % 1024);
+  CK(launch_gemv(L.type, a, ctx->stream, true, ctx->sm_count));
+  return WGD_OK;
+}
+
+// Sum of this rank's partial [n][H] into `hidden` across the tensor-parallel group.
+static int tp_reduce_add(wgd_ctx *ctx, const float *partial, float *hidden, int n) {
+  if (ctx->tp_size == 1) { CK(launch_add(partial, hidden, (int64_t)n * ctx->c.hidden, ctx->stream, true)); return WGD_OK; }
+  return tp_allreduce_add(ctx->tp, partial, hidden, (size_t)n * ctx->c.hidden, ctx->stream, ctx->tp_spin_limit, &g_err);
+}
+
+// Enqueues one forward of n rows (positions from *d_start) on ctx->stream.
+static int enqueue_forward(wgd_ctx *ctx, int n, bool want_logits_rows) {
+  const wgd_model_config &c = ctx->c;
+  const int H = c.hidden, hd = c.head_dim;
+  const bool gemma = c.family == 1, tp1 = ctx->tp_size == 1;
+  int rc;
+  ctx->gemv_slot = 0;
+  CK(cudaMemcpyAsync(ctx->d_start, ctx->h_io, sizeof(int32_t), cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaMemcpyAsync(ctx->d_ids, ctx->h_io + 2, sizeof(int32_t) * n, cudaMemcpyHostToDevice, ctx->stream));
+  CK(launch_embed(ctx->embd.type, ctx->embd.w, ctx->embd.drow, H, ctx->d_ids, n, c.vocab, gemma ? sqrtf((float)H) : 1.f,
+                  ctx->hidden, H, ctx->d_err, ctx->stream, false));
+  for (int l = 0; l < c.layers; l++) {
+    Layer &L = ctx->layers[l];
+    if ((rc = gemv(ctx, L.qkv, ctx->hidden, H, L.attn_norm, ctx->qkv, ctx->qkv_rows, L.qkv_bias, EPI_STORE, n))) return rc;
+    RopeArgs ra{};
+    ra.qkv = ctx->qkv;
+    ra.ld = ctx->qkv_rows;
+    ra.n = n;
+    ra.heads = ctx->heads_l;
+    ra.kv_heads = ctx->kv_l;
+    ra.hd = hd;
+    const bool qkn = gemma || c.qk_norm;
+    ra.rot = gemma ? hd : (c.rotary_dim ? c.rotary_dim : hd);
+    ra.mode = qkn ? 0 : c.rope_mode;
+    ra.q_norm = L.q_norm;
+    ra.k_norm = L.k_norm;
+    ra.eps = c.epsilon;
+    ra.theta = L.theta;
+    ra.scale = L.rope_scale;
+    ra.start = ctx->d_start;
+    ra.k_cache = L.k_cache;
+    ra.v_cache = L.v_cache;
+    ra.capacity = L.capacity;
+    ra.q_out = ctx->qrot;
+    CK(launch_rope_kv(ra, ctx->stream, true));
+    AttnArgs aa{};
+    aa.q = ctx->qrot;
+    aa.k = L.k_cache;
+    aa.v = L.v_cache;
+    aa.out = ctx->att;
+    aa.n = n;
+    aa.heads = ctx->heads_l;
+    aa.kv_heads = ctx->kv_l;
+    aa.hd = hd;
+    aa.capacity = L.capacity;
+    aa.window = L.window;
+    aa.scale = c.attention_scale;
+    aa.start = ctx->d_start;
+    aa.part = ctx->att_part;
+    aa.ctr = ctx->att_ctr;
+    aa.splits = ctx->att_splits;
+    CK(launch_attention(aa, ctx->stream, true));
+    if (gemma) {
+      if ((rc = gemv(ctx, L.o, ctx->att, ctx->q_l, nullptr, ctx->proj, H, nullptr, EPI_STORE, n))) return rc;
+      if (!tp1 && (rc = tp_allreduce_inplace(ctx->tp, ctx->proj, (size_t)n * H, ctx->stream, ctx->tp_spin_limit, &g_err))) return rc;
+      CK(launch_rmsnorm(ctx->proj, H, L.post_attn, c.epsilon, H, n, ctx->hidden, H, 1, ctx->stream, true));
+    } else if (tp1) {
+      if ((rc = gemv(ctx, L.o, ctx->att, ctx->q_l, nullptr, ctx->hidden, H, L.o_bias, EPI_ADD, n))) return rc;
+    } else {
+      if ((rc = gemv(ctx, L.o, ctx->att, ctx->q_l, nullptr, ctx->proj, H, L.o_bias, EPI_STORE, n))) return rc;
+      if ((rc = tp_reduce_add(ctx, ctx->proj, ctx->hidden, n))) return rc;
+    }
+    const bool gated = gemma || c.ffn_gate;
+    const int epi = !gated ? EPI_SILU : (c.activation == 1 || gemma) ? EPI_GLU_GELU : EPI_GLU_SILU;
+    if ((rc = gemv(ctx, L.gate_up, ctx->hidden, H, L.ffn_norm, ctx->act, ctx->ffn_l, nullptr, epi, n))) return rc;
+    if (gemma) {
+      if ((rc = gemv(ctx, L.down, ctx->act, ctx->ffn_l, nullptr, ctx->proj, H, nullptr, EPI_STORE, n))) return rc;
+      if (!tp1 && (rc = tp_allreduce_inplace(ctx->tp, ctx->proj, (size_t)n * H, ctx->stream, ctx->tp_spin_limit, &g_err))) return rc;
+      CK(launch_rmsnorm(ctx->proj, H, L.post_ffw, c.epsilon, H, n, ctx->hidden, H, 1, ctx->stream, true));
+    } else if (tp1) {
+      if ((rc = gemv(ctx, L.down, ctx->act, ctx->ffn_l, nullptr, ctx->hidden, H, nullptr, EPI_ADD, n))) return rc;
+    } else {
+      if ((rc = gemv(ctx, L.down, ctx->act, ctx->ffn_l, nullptr, ctx->proj, H, nullptr, EPI_STORE, n))) return rc;
+      if ((rc = tp_reduce_add(ctx, ctx->proj, ctx->hidden, n))) return rc;
+    }
+  }
+  // LM head on the last row (engine.ts:177-178), then greedy argmax (engine.ts:305-309).
+  float *logits_l = ctx->logits + ctx->vocab0;
+  if ((rc = gemv(ctx, ctx->lm, ctx->hidden + (int64_t)(n - 1) * H, H, ctx->out_norm, logits_l, ctx->vocab_l, nullptr, EPI_STORE, 1)))
+    return rc;
+  CK(launch_argmax(logits_l, ctx->vocab_l, ctx->d_argmax, ctx->d_maxval, ctx->am_part, ctx->am_ctr, ctx->stream, true));
+  if (!tp1) {
+    if ((rc = tp_argmax_gather(ctx->tp, ctx->d_argmax, ctx->d_maxval, ctx->vocab0, ctx->stream, ctx->tp_spin_limit, &g_err))) return rc;
+    if (want_logits_rows &&
+        (rc = tp_gather_rows(ctx->tp, ctx->logits, ctx->c.vocab, ctx->vocab0, ctx->vocab_l, ctx->stream, ctx->tp_spin_limit, &g_err)))
+      return rc;
+  }
+  CK(cudaMemcpyAsync(ctx->h_io + 1, ctx->d_argmax, sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream));
+  return WGD_OK;
+}
+
+extern "C" int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, int want, int32_t *argmax_out, float *logits_out) {
+  if (!ctx || !ids) return fail(WGD_EINVAL, "null argument");
+  if (!ctx->ended) return fail(WGD_ESTATE, "Load a model first.");
+  std::string missing;
+  if (!all_uploaded(ctx, &missing)) return fail(WGD_ESTATE, "weights not uploaded: " + missing);
+  if (n < 1 || n > ctx->max_batch) return fail(WGD_EINVAL, "forward batch must be 1..max_batch");
+  if (start < 0 || start + n > ctx->context) return fail(WGD_EINVAL, "positions exceed the context length");
+  if (want < 0 || want > 2) return fail(WGD_EINVAL, "want must be 0, 1 or 2");
+  for (int i = 0; i < n; i++)
+    if (ids[i] < 0 || ids[i] >= ctx->c.vocab) return fail(WGD_EINVAL, "token id out of range");
+  if (ctx->cancel.exchange(0)) return fail(WGD_ECANCELLED, "Stopped by user");
+  CK(cudaSetDevice(ctx->device));
+  ctx->h_io[0] = start;
+  memcpy(ctx->h_io + 2, ids, sizeof(int32_t) * n);
+  CK(cudaEventRecord(ctx->ev0, ctx->stream));
+  int rc;
+  const bool gather_logits = want == 2;
+  if (n == 1 && ctx->graphs && !gather_logits) {
+    if (!ctx->decode_exec) {
+      CK(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+      rc = enqueue_forward(ctx, 1, false);
+      cudaGraph_t g = nullptr;
+      cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+      if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+      if (e != cudaSuccess) return fail(WGD_ECUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+      ctx->decode_graph = g;
+      CK(cudaGraphInstantiate(&ctx->decode_exec, g, 0));
+    }
+    CK(cudaGraphLaunch(ctx->decode_exec, ctx->stream));
+  } else {
+    if ((rc = enqueue_forward(ctx, n, gather_logits))) return rc;
+  }
+  CK(cudaEventRecord(ctx->ev1, ctx->stream));
+  if (want == 2 && logits_out) {
+    if (ctx->tp_rank == 0) CK(cudaMemcpyAsync(logits_out, ctx->logits, sizeof(float) * ctx->c.vocab, cudaMemcpyDeviceToHost, ctx->stream));
+  }
+  CK(cudaStreamSynchronize(ctx->stream));
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, ctx->ev0, ctx->ev1);
+  ctx->st.last_forward_ms = ms;
+  ctx->st.forwards++;
+  ctx->st.tokens += n;
+  if (ctx->tp && tp_failed(ctx->tp)) return fail(WGD_ETIMEOUT, "a tensor-parallel peer did not answer within the wait limit");
+  if (want >= 1) {
+    if (ctx->h_io[1] < 0) return fail(WGD_ENONFINITE, "Inference produced non-finite logits. Stop and report this model/runtime combination.");
+    if (argmax_out) *argmax_out = ctx->h_io[1];
+  }
+  return WGD_OK;
+}
+
+extern "C" int wgd_truncate_kv(wgd_ctx *ctx, int n_tokens) {
+  if (!ctx) return fail(WGD_EINVAL, "null context");
+  if (n_tokens < 0 || n_tokens > ctx->context) return fail(WGD_EINVAL, "token count outside the context");
+  return WGD_OK;  // positions are explicit in every forward; later positions are overwritten
+}
+
+extern "C" void wgd_cancel(wgd_ctx *ctx) {
+  if (ctx) ctx->cancel.store(1);
+}
+
+extern "C" int wgd_stats_get(wgd_ctx *ctx, wgd_stats *out) {
+  if (!ctx || !out) return fail(WGD_EINVAL, "null argument");
+  ctx->st.gpu_bytes = ctx->allocated;
+  ctx->st.peak_gpu_bytes = ctx->peak;
+  *out = ctx->st;
+  return WGD_OK;
+}
+
+extern "C" int wgd_set_graphs(wgd_ctx *ctx, int enabled) {
+  if (!ctx) return fail(WGD_EINVAL, "null context");
+  ctx->graphs = enabled != 0;
+  return WGD_OK;
+}
+
+// ------------------------------------------------------------ tensor parallel
+
+extern "C" int wgd_tp_handle_size(void) { return tp_handle_size(); }
+extern "C" int wgd_tp_export(wgd_ctx *ctx, void *out) {
+  if (!ctx || !out) return fail(WGD_EINVAL, "null argument");
+  if (!ctx->tp) return fail(WGD_ESTATE, "tensor parallelism needs tp_size > 1 and model_end first");
+  CK(cudaSetDevice(ctx->device));
+  return tp_export(ctx->tp, out, &g_err);
+}
+extern "C" int wgd_tp_open_peers(wgd_ctx *ctx, const void *handles) {
+  if (!ctx || !handles) return fail(WGD_EINVAL, "null argument");
+  if (!ctx->tp) return fail(WGD_ESTATE, "tensor parallelism needs tp_size > 1 and model_end first");
+  CK(cudaSetDevice(ctx->device));
+  return tp_open(ctx->tp, handles, &g_err);
+}
+extern "C" int wgd_tp_set_timeout(wgd_ctx *ctx, uint64_t spin_limit) {
+  if (!ctx) return fail(WGD_EINVAL, "null context");
+  ctx->tp_spin_limit = spin_limit;
+  return WGD_OK;
+}
+
+// ------------------------------------------------------------------ op entry points
+
+namespace {
+std::mutex g_op_mu;
+unsigned *g_op_ctr[16] = {nullptr};
+float *g_op_part[16] = {nullptr};
+size_t g_op_part_n[16] = {0};
+int g_op_sm[16] = {0};
+
+int op_scratch(unsigned **ctr, int *sm) {
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 16) return fail(WGD_EINVAL, "device index");
+  std::lock_guard<std::mutex> lk(g_op_mu);
+  if (!g_op_ctr[dev]) {
+    CK(cudaMalloc(&g_op_ctr[dev], sizeof(unsigned) * 4096));
+    CK(cudaMemset(g_op_ctr[dev], 0, sizeof(unsigned) * 4096));
+    cudaDeviceProp p;
+    CK(cudaGetDeviceProperties(&p, dev));
+    g_op_sm[dev] = p.multiProcessorCount;
+  }
+  *ctr = g_op_ctr[dev];
+  *sm = g_op_sm[dev];
+  return WGD_OK;
+}
+int op_part(size_t floats, float **out) {
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_op_mu);
+  if (g_op_part_n[dev] < floats) {
+    if (g_op_part[dev]) cudaFree(g_op_part[dev]);
+    CK(cudaMalloc(&g_op_part[dev], floats * sizeof(float)));
+    g_op_part_n[dev] = floats;
+  }
+  *out = g_op_part[dev];
+  return WGD_OK;
+}
+}  // namespace
+
+extern "C" int64_t wgd_dev_row_bytes(int type, int64_t cols) {
+  if (!type_supported(type) || cols % block_elems(type)) return -1;
+  return dev_row_bytes(type, cols);
+}
+
+extern "C" int wgd_op_repack(int type, int64_t rows, int64_t cols, const void *raw, void *packed, void *stream) {
+  if (!type_supported(type) || cols % block_elems(type) || rows < 0) return fail(WGD_EINVAL, "bad type or shape");
+  RowMap m{0, (int)rows, 0, 0, 0};
+  CK(launch_repack(type, (const uint8_t *)raw, gguf_row_bytes(type, cols), 0, (int)rows, 0, (int)(cols / block_elems(type)),
+                   (uint8_t *)packed, dev_row_bytes(type, cols), m, (cudaStream_t)stream));
+  return WGD_OK;
+}
+
+extern "C" int wgd_op_dequant(int type, int64_t rows, int64_t cols, const void *packed, float *out, void *stream) {
+  if (!type_supported(type) || cols % block_elems(type)) return fail(WGD_EINVAL, "bad type or shape");
+  CK(launch_dequant(type, (const uint8_t *)packed, dev_row_bytes(type, cols), (int)rows, (int)cols, out, cols, (cudaStream_t)stream));
+  return WGD_OK;
+}
+
+extern "C" int wgd_op_gemv(int type, int64_t rows, int64_t cols, const void *packed, const float *x, int batch, float *y,
+                           void *stream) {
+  if (!type_supported(type) || cols % block_elems(type) || cols % 32 || rows < 1 || batch < 1)
+    return fail(WGD_EINVAL, "bad type, shape or batch");
+  if (gemv_max_batch((int)cols) == 0) return fail(WGD_EINVAL, "matrix too wide for the GEMV kernel");
+  unsigned *ctr;
+  int sm, rc;
+  if ((rc = op_scratch(&ctr, &sm))) return rc;
+  GemvArgs a{};
+  a.w = (const uint8_t *)packed;
+  a.drow = dev_row_bytes(type, cols);
+  a.rows = (int)rows;
+  a.cols = (int)cols;
+  a.nb = (int)(cols / block_elems(type));
+  a.x = x;
+  a.ldx = (int)cols;
+  a.y = y;
+  a.ldy = (int)rows;
+  a.epi = EPI_STORE;
+  a.batch = batch;
+  a.ctr = ctr;
+  CK(launch_gemv(type, a, (cudaStream_t)stream, false, sm));
+  return WGD_OK;
+}
+
+extern "C" int wgd_op_rmsnorm(const float *x, const float *w, int cols, int n, float eps, float *y, void *stream) {
+  CK(launch_rmsnorm(x, cols, w, eps, cols, n, y, cols, 0, (cudaStream_t)stream, false));
+  return WGD_OK;
+}
+
+extern "C" int wgd_op_rope(float *x, const float *norm_w, int n, int heads, int hd, int start, float theta, float scale, float eps,
+                           int rotary_dim, int mode, void *stream) {
+  if (hd % 2 || rotary_dim % 2 || rotary_dim > hd || heads < 1 || n < 1) return fail(WGD_EINVAL, "bad rope shape");
+  RopeArgs a{};
+  a.qkv = x;
+  a.ld = heads * hd;
+  a.n = n;
+  a.heads = heads;
+  a.kv_heads = 0;
+  a.hd = hd;
+  a.rot = rotary_dim ? rotary_dim : hd;
+  a.mode = norm_w ? 0 : mode;
+  a.q_norm = norm_w;
+  a.eps = eps;
+  a.theta = theta;
+  a.scale = scale;
+  a.start_host = start;
+  a.capacity = 1;
+  a.q_out = x;
+  CK(launch_rope_kv(a, (cudaStream_t)stream, false));
+  return WGD_OK;
+}
+
+extern "C" int wgd_op_attention(const float *q, const float *k, const float *v, float *out, int n, int heads, int kv_heads, int hd,
+                                int start, float scale, int window, int capacity, void *stream) {
+  if (n < 1 || heads < 1 || kv_heads < 1 || heads % kv_heads || heads / kv_heads > 8 || hd % 4 || hd > 512 || capacity < 1 ||
+      window < 1 || start < 0)
+    return fail(WGD_EINVAL, "bad attention shape");
+  unsigned *ctr;
+  int sm, rc;
+  if ((rc = op_scratch(&ctr, &sm))) return rc;
+  AttnArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.out = out;
+  a.n = n;
+  a.heads = heads;
+  a.kv_heads = kv_heads;
+  a.hd = hd;
+  a.capacity = capacity;
+  a.window = window;
+  a.scale = scale;
+  a.start_host = start;
+  a.splits = attention_splits(std::min(window, start + n));
+  if (n * kv_heads > 2048) return fail(WGD_EINVAL, "too many attention rows for the op scratch");
+  float *part;
+  if ((rc = op_part(attention_part_floats(n, heads, kv_heads, hd, a.splits), &part))) return rc;
+  a.part = part;
+  a.ctr = ctr + 2048;
+  CK(launch_attention(a, (cudaStream_t)stream, false));
+  return WGD_OK;
+}
+
+extern "C" int wgd_op_argmax(const float *x, int n, int32_t *idx, void *stream) {
+  if (n < 1) return fail(WGD_EINVAL, "empty input");
+  unsigned *ctr;
+  int sm, rc;
+  if ((rc = op_scratch(&ctr, &sm))) return rc;
+  float *part;
+  if ((rc = op_part(2 * 256 + 4, &part))) return rc;
+  CK(launch_argmax(x, n, idx, nullptr, part, ctr + 4000, (cudaStream_t)stream, false));
+  return WGD_OK;
+}

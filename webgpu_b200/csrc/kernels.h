@@ -1,0 +1,110 @@
+// Host-side launchers of the wgd CUDA kernels (internal; the public C ABI is include/wgd.h).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace wgd {
+
+// ------------------------------------------------------------------ GEMV
+// y[b, row] (op) acc(b, row) for the output rows of a weight matrix stored in the
+// device row layout. Rows are processed in items of 4; `ctr` points to two
+// zeroed uint32 (work ticket, finished CTAs) private to this launch site; the
+// kernel leaves them zeroed again.
+enum Epi : int {
+  EPI_STORE = 0,     // y = acc + bias
+  EPI_ADD = 1,       // y += acc + bias            (residual add)
+  EPI_SILU = 2,      // y = silu(acc + bias)       (ungated MLP up projection)
+  EPI_GLU_SILU = 3,  // rows interleaved [g g u u]: y = silu(g) * u
+  EPI_GLU_GELU = 4,  // rows interleaved [g g u u]: y = gelu_tanh(g) * u
+};
+constexpr int GEMV_ROWS = 4;  // rows per work item; GLU interleave is 2 gate + 2 up rows
+
+struct GemvArgs {
+  const uint8_t *w;   // device-layout weights
+  int64_t drow;       // bytes per device row
+  int rows, cols;     // device rows (GLU: gate+up rows), columns
+  int nb;             // blocks per row (for the scale arrays of Q4_0/Q8_0/Q6_K)
+  const float *x;     // activations [batch][ldx]
+  int ldx;
+  const float *norm_w;  // non-null: x is RMS-normalised with this weight first
+  float eps;
+  float *y;
+  int ldy;
+  const float *bias;  // [rows] in device row order, or null
+  int epi;
+  int batch;          // number of activation rows
+  unsigned *ctr;      // 2 x uint32, zero on entry and on exit
+};
+cudaError_t launch_gemv(int type, const GemvArgs &a, cudaStream_t s, bool pdl, int sm_count);
+// Largest batch chunk the register-resident GEMV handles for this width in one pass.
+int gemv_max_batch(int cols);
+
+// --------------------------------------------------------------- layout
+// Raw GGUF rows -> device rows. Source rows [0, nrows) at `src` (row stride
+// `src_row_bytes`); block columns [blk0, blk0 + nbl) of each row are moved to
+// destination row dst_row(r) = map(r0 + r) (see RowMap).
+struct RowMap {
+  int src_begin;   // first source row kept (global row index)
+  int src_end;     // one past the last kept row
+  int dst_base;    // logical destination row of src_begin
+  int interleave;  // 0: plain; 1: gate part; 2: up part (GLU interleave of 2)
+  int glu_rows;    // logical rows of one GLU part (for interleave)
+};
+cudaError_t launch_repack(int type, const uint8_t *src, int64_t src_row_bytes, int row0, int nrows, int blk0, int nbl,
+                          uint8_t *dst, int64_t dst_row_bytes, RowMap map, cudaStream_t s);
+cudaError_t launch_dequant(int type, const uint8_t *w, int64_t drow, int rows, int cols, float *out, int64_t ldo,
+                           cudaStream_t s);
+// Dequantises selected rows (ids[t]) scaled by `scale` into out[t][cols] (embedding gather).
+cudaError_t launch_embed(int type, const uint8_t *w, int64_t drow, int cols, const int *ids, int n, int vocab, float scale,
+                         float *out, int ldo, int *err, cudaStream_t s, bool pdl);
+
+// ---------------------------------------------------------- block ops
+// RMS norm of x rows (n rows of `cols`) with weight w: y = x * rsqrt(mean(x^2)+eps) * w.
+// add != 0: y += (normed value) instead (Gemma post-norm residual).
+cudaError_t launch_rmsnorm(const float *x, int ldx, const float *w, float eps, int cols, int n, float *y, int ldy, int add,
+                           cudaStream_t s, bool pdl);
+
+struct RopeArgs {
+  float *qkv;          // [n][ld] rows: q heads, then k heads, then v heads (hd each)
+  int ld;
+  int n, heads, kv_heads, hd;
+  int rot;             // rotary dims (even, <= hd)
+  int mode;            // 0 half-split, 1 adjacent pairs
+  const float *q_norm, *k_norm;  // per-head RMS weights (qk-norm) or null
+  float eps;
+  double theta, scale;
+  const int *start;    // device int: absolute position of row 0
+  int start_host;      // used when start == nullptr
+  float *k_cache, *v_cache;  // [kv_heads][capacity][hd]
+  int capacity;
+  float *q_out;        // [n][heads][hd]
+};
+cudaError_t launch_rope_kv(const RopeArgs &a, cudaStream_t s, bool pdl);
+
+struct AttnArgs {
+  const float *q;      // [n][heads][hd]
+  const float *k, *v;  // [kv_heads][capacity][hd]
+  float *out;          // [n][heads][hd]
+  int n, heads, kv_heads, hd, capacity, window;
+  float scale;
+  const int *start;    // device int or null (then start_host)
+  int start_host;
+  float *part;         // scratch: [n][kv_heads][splits][group*(hd+2)]
+  unsigned *ctr;       // [n * kv_heads] zeroed counters (left zeroed)
+  int splits;          // grid.y
+};
+cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl);
+int attention_splits(int max_len);
+size_t attention_part_floats(int n, int heads, int kv_heads, int hd, int splits);
+
+// Argmax over finite values of x[0..n) (first index wins ties). Writes
+// out_idx (int, -1 when nothing is finite) and out_val. `part` holds
+// 2*blocks floats; ctr one zeroed uint32.
+cudaError_t launch_argmax(const float *x, int n, int *out_idx, float *out_val, float *part, unsigned *ctr, cudaStream_t s,
+                          bool pdl);
+int argmax_blocks(int n);
+
+// Elementwise: y += x (n floats).
+cudaError_t launch_add(const float *x, float *y, int64_t n, cudaStream_t s, bool pdl);
+
+}  // namespace wgd

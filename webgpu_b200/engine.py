@@ -1,0 +1,405 @@
+"""PagedEngine: the host half of the decoder loop.
+
+A mirror of the reference's PagedEngine (src/core/engine.ts:26-304,
+ahpah-dev/WebGPU 0.9.0): the same presets, option validation, prefix reuse,
+prompt-batch prefill, streamed greedy/temperature generation and error
+messages. The device half — WebGPU buffers, WGSL dispatches and weight-page
+uploads — is replaced by the CUDA library (include/wgd.h), called once per
+forward.
+
+Deliberate differences, for a B200 host: the GPU budget ceiling is the device's
+memory (the reference caps it at a browser's 16 GiB); `LoadOptions` adds
+`tensorParallel`/`rank`/`device`/`exchange` for multi-GPU runs; `generate_ids`
+drives token ids directly (no tokenizer), which the benchmark configurations use.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import random
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import _native
+from .context import MAX_CONTEXT, MAX_MESSAGE_CHARS, attention_memory, output_limit, suggest_budget, validate_context
+from .gguf import model_config, read_gguf, to_native_config
+from .source import make_source
+
+MiB = 1024 ** 2
+# engine.ts:14-18
+PRESETS = {"lite": {"budget": 512, "batch": 8, "page": 16},
+           "low-memory": {"budget": 2048, "batch": 16, "page": 16},
+           "fast": {"budget": 6144, "batch": 128, "page": 64}}
+MAX_BUDGET_MIB = 180 * 1024  # one B200's HBM; the browser reference stops at 16384
+
+
+class AbortError(Exception):
+    """Raised when a request is cancelled (the reference's AbortError, sdk.ts:27)."""
+
+
+@dataclass
+class TokenEvent:
+    """engine.ts:24"""
+    token: int
+    text: str
+    delta: str
+    tokens: int
+    promptTokens: int
+    contextLength: int
+    seconds: float
+    stats: dict
+
+
+@dataclass
+class ModelInfo:
+    """engine.ts:23"""
+    config: object
+    fileBytes: int
+    adapter: str
+    contextLength: int
+    gpuBudgetMiB: int
+    batchSize: int
+    performance: str
+    stats: dict
+    tensorParallel: int = 1
+
+
+class ByteTokenizer:
+    """Byte-alphabet chat framing of the reference's dense check models
+    (scripts/verify-dense.mjs:54-58,212-220): token id = UTF-8 byte, plus
+    <|im_start|>/<|im_end|> specials. Full BPE tokenizers are host code the
+    reference keeps unchanged; they are not part of this runtime."""
+
+    def __init__(self, metadata: dict):
+        tokens = metadata.get("tokenizer.ggml.tokens") or []
+        self.tokens = tokens
+        self.start = tokens.index("<|im_start|>") if "<|im_start|>" in tokens else None
+        self.end = tokens.index("<|im_end|>") if "<|im_end|>" in tokens else None
+        eos = metadata.get("tokenizer.ggml.eos_token_id")
+        self.eos = {int(eos)} if eos is not None else set()
+        self.alphabet = {ch: i for i, ch in enumerate(tokens[:256])} if len(tokens) >= 256 else {}
+
+    @property
+    def usable(self) -> bool:
+        return self.start is not None and self.end is not None and len(self.alphabet) == 256
+
+    def chat(self, messages) -> list[int]:
+        if not self.usable:
+            raise ValueError("This model's tokenizer is not available in this host; use generate_ids.")
+        ids: list[int] = []
+        for m in messages:
+            ids += [self.start, *f"{m['role']}\n".encode(), *m["content"].strip().encode(), self.end, *b"\n"]
+        ids += [self.start, *b"assistant\n"]
+        return ids
+
+    def decode(self, ids) -> str:
+        inv = {i: ch for ch, i in self.alphabet.items()}
+        rev = {}
+        # GPT-2 byte alphabet back to bytes
+        kept = [b for b in range(256) if 33 <= b <= 126 or 161 <= b <= 172 or b >= 174]
+        extra = 256
+        for b in range(256):
+            if b in kept:
+                rev[chr(b)] = b
+            else:
+                rev[chr(extra)] = b
+                extra += 1
+        out = bytearray()
+        for i in ids:
+            ch = inv.get(i)
+            if ch is not None and ch in rev:
+                out.append(rev[ch])
+        return out.decode("utf-8", errors="replace")
+
+
+def sample(logits: np.ndarray, temperature: float, top_k: int, top_p: float, rng=random) -> int:
+    """engine.ts:305-324."""
+    x = np.asarray(logits, dtype=np.float64)
+    finite = np.isfinite(x)
+    if not finite.any():
+        raise ValueError("Inference produced non-finite logits. Stop and report this model/runtime combination.")
+    masked = np.where(finite, x, -np.inf)
+    best_id = int(np.argmax(masked))
+    best = masked[best_id]
+    if temperature == 0:
+        return best_id
+    order = np.argsort(-masked, kind="stable")
+    cand = [int(i) for i in order[:top_k] if finite[i]]
+    probs = [math.exp((x[i] - best) / temperature) for i in cand]
+    total = sum(probs)
+    retained, cutoff = 0.0, 0
+    while cutoff < len(cand):
+        retained += probs[cutoff]
+        if retained / total >= top_p:
+            cutoff += 1
+            break
+        cutoff += 1
+    draw = rng.random() * retained
+    for i in range(cutoff):
+        draw -= probs[i]
+        if draw <= 0:
+            return cand[i]
+    return best_id
+
+
+class PagedEngine:
+    def __init__(self, progress=None):
+        self.progress = progress or (lambda p: None)
+        self.ctx = None
+        self.source = None
+        self.gguf = None
+        self.config = None
+        self.tokenizer = None
+        self.context = 512
+        self.batch = 16
+        self.budget = 2048
+        self.performance = "low-memory"
+        self.busy = False
+        self.disposed = False
+        self.tokens_in_cache: list[int] = []
+        self.kv_capacities: list[int] = []
+        self.tp = 1
+        self.rank = 0
+        self.device = 0
+        self._logits = None
+
+    # ------------------------------------------------------------------ load
+    def load(self, src, options: dict | None = None, signal=None) -> ModelInfo:
+        """engine.ts:51-114."""
+        o = dict(options or {})
+        self.performance = o.get("performance", "low-memory")
+        if self.performance not in PRESETS:
+            raise ValueError("Performance must be lite, low-memory or fast.")
+        preset = PRESETS[self.performance]
+        self.context = o.get("contextLength", 512)
+        self.batch = o.get("batchSize", preset["batch"])
+        validate_context(self.context)
+        if self.batch not in (1, 8, 16, 32, 64, 128):
+            raise ValueError("Batch size must be 1, 8, 16, 32, 64 or 128.")
+        b = o.get("gpuBudgetMiB")
+        if b is not None and (not isinstance(b, int) or b < 512 or b > MAX_BUDGET_MIB):
+            raise ValueError(f"GPU budget must be 512–{MAX_BUDGET_MIB} MiB.")
+        self.tp = int(o.get("tensorParallel", 1))
+        self.rank = int(o.get("rank", 0))
+        self.device = int(o.get("device", self.rank))
+        self.source = make_source(src)
+        self.progress({"phase": "loading", "detail": "Reading GGUF metadata and tokenizer", "fraction": 0.05})
+        self.gguf = read_gguf(self.source)
+        self.config = c = model_config(self.gguf)
+        validate_context(self.context, c.max_context)
+        self.budget = b if b is not None else suggest_budget(self.source.size, self.performance)
+        if not isinstance(self.budget, int) or self.budget < 512 or self.budget > MAX_BUDGET_MIB:
+            raise ValueError(f"GPU budget must be 512–{MAX_BUDGET_MIB} MiB.")
+        self.tokenizer = ByteTokenizer(self.gguf.metadata)
+        memory = attention_memory(c, self.context, self.batch)
+        self.kv_capacities = memory["capacities"]
+        kv_per_rank = memory["total_bytes"] // self.tp
+        if kv_per_rank + 256 * MiB > self.budget * MiB:
+            raise ValueError(f"A {self.context:,}-token context needs {math.ceil(kv_per_rank / MiB):,} MiB of attention state "
+                             f"plus working memory. Choose at least {math.ceil((kv_per_rank + 256 * MiB) / MiB):,} MiB of GPU "
+                             f"budget, or reduce context.")
+        L = _native.lib()
+        status = ctypes.c_int(0)
+        self.ctx = L.wgd_create(self.device, self.rank, self.tp, self.budget * MiB, preset["page"] * MiB, ctypes.byref(status))
+        if not self.ctx:
+            _native.check(status.value, "wgd_create")
+        try:
+            self.progress({"phase": "loading", "detail": "Placing weights on the GPU", "fraction": 0.25})
+            cfg = to_native_config(c)
+            _native.check(L.wgd_model_begin(self.ctx, ctypes.byref(cfg), self.context, self.batch), "model_begin")
+            for t in self.gguf.tensors.values():
+                dims = (ctypes.c_uint64 * 4)(*t.dims, *([0] * (4 - len(t.dims))))
+                _native.check(L.wgd_tensor_register(self.ctx, t.name.encode(), t.type, dims, len(t.dims), t.offset, t.bytes,
+                                                    t.row_bytes), "tensor_register")
+            _native.check(L.wgd_model_end(self.ctx), "model_end")
+            if self.tp > 1:
+                self._open_peers(o.get("exchange"))
+            self._upload(signal)
+            ready = ctypes.c_int(0)
+            _native.check(L.wgd_model_ready(self.ctx, ctypes.byref(ready)), "model_ready")
+            if not ready.value:
+                raise RuntimeError("weights incomplete after load")
+            self.progress({"phase": "ready", "detail": "Ready.", "fraction": 1.0, "stats": self.stats()})
+            return self.info()
+        except BaseException:
+            self.dispose()
+            raise
+
+    def _open_peers(self, exchange):
+        """Exchanges the device handles of the tensor-parallel exchange buffers.
+        `exchange(bytes) -> list[bytes]` is an all-gather over the ranks."""
+        if exchange is None:
+            raise ValueError("tensorParallel > 1 needs an 'exchange' all-gather callable")
+        L = _native.lib()
+        n = L.wgd_tp_handle_size()
+        buf = ctypes.create_string_buffer(n)
+        _native.check(L.wgd_tp_export(self.ctx, buf), "tp_export")
+        handles = exchange(bytes(buf.raw))
+        if len(handles) != self.tp:
+            raise RuntimeError("handle exchange returned the wrong number of ranks")
+        allh = b"".join(handles)
+        _native.check(L.wgd_tp_open_peers(self.ctx, ctypes.c_char_p(allh)), "tp_open_peers")
+
+    def _upload(self, signal=None):
+        L = _native.lib()
+        view = self.source.view()
+        tensors = list(self.gguf.tensors.values())
+        for i, t in enumerate(tensors):
+            if signal is not None and signal.is_set():
+                raise AbortError("Stopped by user")
+            if view is not None:
+                ptr = view.ctypes.data + t.offset
+                if t.bytes <= 64 * MiB or len(t.dims) == 1:
+                    _native.check(L.wgd_tensor_upload(self.ctx, t.name.encode(), 0, ctypes.c_void_p(ptr), t.bytes), "upload")
+                else:
+                    step = max(1, (64 * MiB) // t.row_bytes) * t.row_bytes
+                    for off in range(0, t.bytes, step):
+                        n = min(step, t.bytes - off)
+                        _native.check(L.wgd_tensor_upload(self.ctx, t.name.encode(), off, ctypes.c_void_p(ptr + off), n), "upload")
+            else:
+                step = max(1, (64 * MiB) // t.row_bytes) * t.row_bytes if len(t.dims) > 1 else t.bytes
+                for off in range(0, t.bytes, step):
+                    n = min(step, t.bytes - off)
+                    data = bytes(self.source.read(t.offset + off, n))
+                    _native.check(L.wgd_tensor_upload(self.ctx, t.name.encode(), off, data, n), "upload")
+            if i % 20 == 0:
+                self.progress({"phase": "loading", "detail": "Uploading weights", "fraction": 0.3 + 0.65 * i / len(tensors)})
+
+    def info(self) -> ModelInfo:
+        return ModelInfo(self.config, self.source.size, "NVIDIA B200 (wgd)", self.context, self.budget, self.batch,
+                         self.performance, self.stats(), self.tp)
+
+    def stats(self) -> dict:
+        """PagingStats (pager.ts:5) plus device timings."""
+        if not self.ctx:
+            return {}
+        s = _native.StatsC()
+        _native.check(_native.lib().wgd_stats_get(self.ctx, ctypes.byref(s)), "stats")
+        return {"readBytes": s.read_bytes, "readMs": s.read_ms, "uploads": s.uploads, "cacheHits": s.cache_hits,
+                "cacheBytes": s.cache_bytes, "gpuBytes": s.gpu_bytes, "peakGpuBytes": s.peak_gpu_bytes,
+                "pageBytes": s.page_bytes, "forwards": s.forwards, "tokens": s.tokens, "lastForwardMs": s.last_forward_ms,
+                "streamedBytes": s.streamed_bytes}
+
+    # --------------------------------------------------------------- forward
+    def forward(self, ids, start: int, logits: bool, want_logits: bool = False):
+        """engine.ts:138-180 — one device call. Returns the greedy token id of the last
+        row (and the logits when want_logits) or None when logits is False."""
+        L = _native.lib()
+        n = len(ids)
+        arr = (ctypes.c_int32 * n)(*ids)
+        out = ctypes.c_int32(-1)
+        want = 0 if not logits else (2 if want_logits else 1)
+        lp = None
+        if want == 2:
+            if self._logits is None:
+                self._logits = np.zeros(self.config.vocab, dtype=np.float32)
+            lp = self._logits.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        st = L.wgd_forward(self.ctx, arr, n, start, want, ctypes.byref(out), lp)
+        if st == _native.WGD_ECANCELLED:
+            raise AbortError("Stopped by user")
+        if st == _native.WGD_ENONFINITE:
+            raise ValueError(_native.last_error())
+        _native.check(st, "forward")
+        if want == 0:
+            return None
+        return (out.value, self._logits.copy()) if want == 2 else out.value
+
+    # --------------------------------------------------------------- generate
+    def generate(self, messages, options: dict | None = None, signal=None):
+        """engine.ts:257-301."""
+        if self.busy:
+            raise RuntimeError("A generation is already running.")
+        if self.disposed or not self.ctx:
+            raise RuntimeError("Load a model first.")
+        if (not isinstance(messages, list) or not messages
+                or any(m.get("role") not in ("user", "assistant") or not isinstance(m.get("content"), str)
+                       or len(m["content"]) > MAX_MESSAGE_CHARS for m in messages)):
+            raise ValueError(f"Provide user/assistant text messages (at most {MAX_MESSAGE_CHARS:,} characters each).")
+        prompt = self.tokenizer.chat(messages)
+        yield from self._generate(prompt, options or {}, signal)
+
+    def generate_ids(self, prompt_ids, options: dict | None = None, signal=None):
+        """Token-id entry point (no tokenizer): the same loop as generate."""
+        if self.busy:
+            raise RuntimeError("A generation is already running.")
+        if self.disposed or not self.ctx:
+            raise RuntimeError("Load a model first.")
+        prompt = [int(i) for i in prompt_ids]
+        if not prompt:
+            raise ValueError("The prompt has no tokens.")
+        yield from self._generate(prompt, options or {}, signal)
+
+    def _generate(self, prompt, options, signal):
+        max_tokens = options.get("maxTokens", 128)
+        if not isinstance(max_tokens, int) or max_tokens < 1 or max_tokens > MAX_CONTEXT:
+            raise ValueError(f"maxTokens must be 1–{MAX_CONTEXT}.")
+        temperature = options.get("temperature", 0.7)
+        top_k = options.get("topK", 40)
+        top_p = options.get("topP", 0.9)
+        if (not math.isfinite(temperature) or temperature < 0 or temperature > 2 or not isinstance(top_k, int) or top_k < 1
+                or top_k > 200 or not math.isfinite(top_p) or top_p <= 0 or top_p > 1):
+            raise ValueError("Invalid sampling settings.")
+        self.busy = True
+        try:
+            limit = output_limit(max_tokens, len(prompt), self.context)
+            shared = 0
+            while shared < len(prompt) and shared < len(self.tokens_in_cache) and prompt[shared] == self.tokens_in_cache[shared]:
+                shared += 1
+            shared = min(shared, len(prompt) - 1)
+            if shared < len(self.tokens_in_cache) and any(cap < self.context for cap in self.kv_capacities):
+                shared = 0
+            started = time.perf_counter()
+            self.tokens_in_cache = self.tokens_in_cache[:shared]
+            greedy = temperature == 0
+            result = None
+            for i in range(shared, len(prompt), self.batch):
+                if signal is not None and signal.is_set():
+                    raise AbortError("Stopped by user")
+                batch = prompt[i:i + self.batch]
+                last = i + len(batch) == len(prompt)
+                result = self.forward(batch, i, last, want_logits=last and not greedy)
+                self.tokens_in_cache += batch
+            generated: list[int] = []
+            text = ""
+            for i in range(limit):
+                if signal is not None and signal.is_set():
+                    raise AbortError("Stopped by user")
+                token = result if greedy else sample(result[1], temperature, top_k, top_p)
+                if token in self.tokenizer.eos:
+                    break
+                generated.append(token)
+                full = self.tokenizer.decode(generated) if self.tokenizer.usable else ""
+                delta = full[len(text):]
+                text = full
+                yield TokenEvent(token, text, delta, len(generated), len(prompt), self.context,
+                                 time.perf_counter() - started, self.stats())
+                if i + 1 < limit:
+                    result = self.forward([token], len(self.tokens_in_cache), True, want_logits=not greedy)
+                    self.tokens_in_cache.append(token)
+        except BaseException:
+            self.tokens_in_cache = []
+            raise
+        finally:
+            self.busy = False
+
+    def reset(self):
+        """engine.ts:302"""
+        if self.busy:
+            raise RuntimeError("Stop generation first.")
+        self.tokens_in_cache = []
+        if self.ctx:
+            _native.lib().wgd_truncate_kv(self.ctx, 0)
+
+    def cancel(self):
+        if self.ctx:
+            _native.lib().wgd_cancel(self.ctx)
+
+    def dispose(self):
+        """engine.ts:303"""
+        self.disposed = True
+        if self.ctx:
+            _native.lib().wgd_destroy(self.ctx)
+            self.ctx = None
+        self.tokens_in_cache = []
