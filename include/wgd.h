@@ -130,6 +130,14 @@ WGD_API int wgd_model_placement(wgd_ctx *ctx, uint64_t *resident_bytes, uint64_t
  * of the last row (engine.ts:305-309), 2 greedy token and full logits of the
  * last row (vocab floats, rank 0 of a TP group). */
 WGD_API int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, int want, int32_t *argmax_out, float *logits_out);
+/* Greedy decode of `steps` tokens entirely on the device: `first` is the token
+ * at position `start`; each step's argmax becomes the next step's input
+ * without a host round trip (the reference's greedy generate loop,
+ * engine.ts:290-297, with sample() on the device). tokens_out receives the
+ * `steps` generated ids (stopping early is the caller's business). */
+WGD_API int wgd_decode(wgd_ctx *ctx, int32_t first, int start, int steps, int32_t *tokens_out);
+/* Number of kernels one single-token forward launches (for launch accounting). */
+WGD_API int wgd_kernels_per_token(wgd_ctx *ctx, int *count);
 /* KV cache bookkeeping for prefix reuse and reset (engine.ts:269-283,302). */
 WGD_API int wgd_truncate_kv(wgd_ctx *ctx, int n_tokens);
 WGD_API void wgd_cancel(wgd_ctx *ctx);
@@ -152,6 +160,16 @@ WGD_API int wgd_op_dequant(int ggml_type, int64_t rows, int64_t cols, const void
  * shaders.ts:68-83; expectation verify.ts:32-35). */
 WGD_API int wgd_op_gemv(int ggml_type, int64_t rows, int64_t cols, const void *packed_dev, const float *x_dev, int batch,
                 float *y_dev, void *stream);
+/* Tile-16 layout used by the tensor-core GEMV for Q4_K / Q6_K matrices (rows
+ * in groups of 16, each GGUF block column of a group stored together so that
+ * mma.sync fragments load with coalesced 16-byte reads). Bytes of a rows x
+ * cols matrix, or -1 if the type/shape has no tiled form. */
+WGD_API int64_t wgd_tiled_bytes(int ggml_type, int64_t rows, int64_t cols);
+WGD_API int wgd_op_repack_tiled(int ggml_type, int64_t rows, int64_t cols, const void *raw_dev, void *tiled_dev, void *stream);
+WGD_API int wgd_op_dequant_tiled(int ggml_type, int64_t rows, int64_t cols, const void *tiled_dev, float *out_dev, void *stream);
+/* The same product as wgd_op_gemv over tiled weights (integer tensor-core path). */
+WGD_API int wgd_op_gemv_tiled(int ggml_type, int64_t rows, int64_t cols, const void *tiled_dev, const float *x_dev, int batch,
+                              float *y_dev, void *stream);
 /* RMSNorm of n rows (normShader, shaders.ts:84-97). */
 WGD_API int wgd_op_rmsnorm(const float *x_dev, const float *w_dev, int cols, int n, float eps, float *y_dev, void *stream);
 /* Q/K rotation (+ optional per-head RMS norm) of x[n][heads][hd] in place:

@@ -140,10 +140,74 @@ void or_dequant_f32(const uint8_t *data, int type, int64_t n, float *out) {
   for (int64_t i = 0; i < n; i++) out[i] = or_decode_weight_f32(data, type, i);
 }
 
-/* Row dequant used by the decoder: one row of `cols` values, f64, identical
- * values to or_decode_weight (same formula per element). */
-static void dequant_row(const uint8_t *row, int type, int64_t cols, double *out) {
-  for (int64_t i = 0; i < cols; i++) out[i] = or_decode_weight(row, type, i);
+/* Row dequant used by the decoder and the matmul: the quant.ts formula of
+ * or_decode_weight per element, with the per-block operands (d, dmin, the
+ * 6-bit scale and min, the int8 scale) hoisted out of the element loop. Every
+ * value is the same expression on the same operands, so the result is
+ * bit-identical to or_decode_weight (checked by or_dequant_row_matches). */
+static void dequant_row(const uint8_t *b, int type, int64_t cols, double *out) {
+#define F16(p) or_half_to_float((uint32_t)b[(p)] | ((uint32_t)b[(p) + 1] << 8))
+  if (type == T_F32) { for (int64_t i = 0; i < cols; i++) { float f; memcpy(&f, b + i * 4, 4); out[i] = f; } return; }
+  if (type == T_F16) { for (int64_t i = 0; i < cols; i++) out[i] = F16(i * 2); return; }
+  if (type == T_Q4_0) {
+    for (int64_t k = 0; k < cols / 32; k++) {
+      int64_t p = k * 18; double d = F16(p);
+      for (int j = 0; j < 32; j++) out[k * 32 + j] = d * (double)(((b[p + 2 + j % 16] >> (j < 16 ? 0 : 4)) & 15) - 8);
+    }
+    return;
+  }
+  if (type == T_Q8_0) {
+    for (int64_t k = 0; k < cols / 32; k++) {
+      int64_t p = k * 34; double d = F16(p);
+      for (int j = 0; j < 32; j++) { int q = b[p + 2 + j]; out[k * 32 + j] = d * (double)(q > 127 ? q - 256 : q); }
+    }
+    return;
+  }
+  if (type == T_Q4_K || type == T_Q5_K) {
+    const int bb = type == T_Q4_K ? 144 : 176, qo = type == T_Q4_K ? 16 : 48;
+    for (int64_t k = 0; k < cols / 256; k++) {
+      int64_t p = k * bb; double d = F16(p), dm = F16(p + 2);
+      for (int s = 0; s < 8; s++) {
+        int sc = s < 4 ? (b[p + 4 + s] & 63) : ((b[p + 8 + s] & 15) | ((b[p + s] >> 6) << 4));
+        int mn = s < 4 ? (b[p + 8 + s] & 63) : ((b[p + 8 + s] >> 4) | ((b[p + 4 + s] >> 6) << 4));
+        for (int jj = 0; jj < 32; jj++) {
+          int j = 32 * s + jj;
+          int q = (b[p + qo + (j / 64) * 32 + j % 32] >> (s % 2 * 4)) & 15;
+          if (type == T_Q5_K) q |= ((b[p + 16 + j % 32] >> s) & 1) << 4;
+          out[k * 256 + j] = d * sc * q - dm * mn;
+        }
+      }
+    }
+    return;
+  }
+  if (type == T_Q6_K) {
+    for (int64_t k = 0; k < cols / 256; k++) {
+      int64_t p = k * 210; double d = F16(p + 208);
+      for (int j = 0; j < 256; j++) {
+        int segment = j / 128, quarter = (j % 128) / 32, lane = j % 32;
+        int low = (b[p + segment * 64 + quarter % 2 * 32 + lane] >> ((quarter / 2) * 4)) & 15;
+        int high = (b[p + 128 + segment * 32 + lane] >> (quarter * 2)) & 3;
+        int scale = b[p + 192 + segment * 8 + quarter * 2 + lane / 16];
+        out[k * 256 + j] = d * (double)(scale > 127 ? scale - 256 : scale) * (double)((low | high << 4) - 32);
+      }
+    }
+    return;
+  }
+#undef F16
+  for (int64_t i = 0; i < cols; i++) out[i] = NAN;
+}
+
+/* 1 when the hoisted row decoder reproduces or_decode_weight bit for bit. */
+int or_dequant_row_matches(const uint8_t *row, int type, int64_t cols) {
+  double *a = (double *)malloc(sizeof(double) * cols);
+  dequant_row(row, type, cols, a);
+  int ok = 1;
+  for (int64_t i = 0; i < cols && ok; i++) {
+    double r = or_decode_weight(row, type, i);
+    ok = memcmp(&a[i], &r, sizeof(double)) == 0;
+  }
+  free(a);
+  return ok;
 }
 
 static int g_threads = 1;

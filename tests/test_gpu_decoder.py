@@ -1,0 +1,184 @@
+"""End-to-end decoder parity on the GPU through the public API (PagedEngine ->
+C ABI) against the float64 CPU oracle decoder, on identical seeded GGUF bytes.
+
+Bars (from the benchmark's north star): greedy tokens identical; logits within
+1e-3 max relative error, measured as max|gpu - oracle| / max|oracle| over the
+vocabulary row (fp32 accumulate path). Models: the reference's three
+verify-dense check models (scripts/verify-dense.mjs:60-135, 4 greedy tokens
+from the chat-framed 'hello' prompt), BASELINE config 1, a Gemma-3 block with
+local/global layers and a ring that wraps, a Mistral-style sliding window, and
+full-width layers of the Qwen2.5-0.5B and Llama-3-8B architectures."""
+import numpy as np
+import pytest
+
+import oracle
+from webgpu_b200 import synth
+from webgpu_b200.engine import PagedEngine
+from webgpu_b200.gguf import model_config, parse_gguf_header
+from webgpu_b200.source import MemorySource
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 1e-3
+
+
+def load(spec, context=512, batch=16, budget=None, image=None):
+    image = synth.build_gguf(spec) if image is None else image
+    e = PagedEngine()
+    opts = {"contextLength": context, "batchSize": batch, "performance": "fast"}
+    if budget:
+        opts["gpuBudgetMiB"] = budget
+    e.load(MemorySource(image), opts)
+    return e, image
+
+
+def oracle_for(image, context, threads=8):
+    g = parse_gguf_header(image, image.nbytes)
+    return oracle.Decoder(image, g, model_config(g), context, threads=threads)
+
+
+def rel(got, exp):
+    return float(np.max(np.abs(got.astype(np.float64) - exp)) / np.max(np.abs(exp)))
+
+
+def compare(spec, steps, context=512, batch=16, prompt=None):
+    e, image = load(spec, context, batch)
+    prompt = list(spec.prompt if prompt is None else prompt)
+    dec = oracle_for(image, context)
+    ref_tokens, ref_logits = dec.greedy_decode(prompt, steps)
+    # GPU: same schedule (prefill in batches of `batch`, then one token per forward)
+    pos, tokens, errs = 0, [], []
+    for i in range(0, len(prompt), batch):
+        chunk = prompt[i:i + batch]
+        out = e.forward(chunk, i, i + len(chunk) == len(prompt), want_logits=True)
+        pos += len(chunk)
+    for s in range(steps):
+        tok, logits = out
+        errs.append(rel(logits, ref_logits[s]))
+        tokens.append(tok)
+        if s + 1 < steps:
+            out = e.forward([tok], pos, True, want_logits=True)
+            pos += 1
+    e.dispose()
+    dec.close()
+    margins = [float(np.sort(l)[-1] - np.sort(l)[-2]) for l in ref_logits]
+    return tokens, ref_tokens, errs, margins
+
+
+@pytest.mark.parametrize("kind", ["llama", "qwen2", "qwen3"])
+def test_verify_dense_models(cuda, kind):
+    tokens, ref, errs, margins = compare(synth.tiny_dense(kind), 4)
+    assert tokens == ref, (tokens, ref, margins)
+    assert max(errs) < LOGIT_TOL, errs
+
+
+def test_baseline_config1_tiny_llama(cuda):
+    tokens, ref, errs, margins = compare(synth.baseline_spec(0), 4, batch=8)
+    assert tokens == ref, (tokens, ref, margins)
+    assert max(errs) < LOGIT_TOL, errs
+
+
+def test_generate_api_matches_oracle_tokens(cuda):
+    spec = synth.tiny_dense("llama")
+    e, image = load(spec)
+    events = list(e.generate([{"role": "user", "content": "hello"}], {"maxTokens": 4, "temperature": 0}))
+    dec = oracle_for(image, 512)
+    ref, _ = dec.greedy_decode(spec.prompt, 4)
+    got = [ev.token for ev in events]
+    # generation stops early only at EOS, exactly as the reference does
+    assert got == ref[:len(got)]
+    e.dispose()
+
+
+def gemma_small(window=6, layers=6):
+    s = synth.gemma_spec(seed=11, layers=layers, hidden=256, ffn=512, heads=4, kv_heads=2, head_dim=64, vocab=300,
+                         window=window, wtype=synth.Q4_K, embd_type=synth.Q6_K, std=0.05)
+    s.prompt = synth.uniform_ids(21, 300, seed=11)
+    return s
+
+
+def test_gemma_block_local_global_and_ring_wrap(cuda):
+    # window 6 with prefill batch 8: local rings hold 13 slots and wrap during the prompt
+    tokens, ref, errs, margins = compare(gemma_small(), 6, batch=8)
+    assert tokens == ref, (tokens, ref, margins)
+    assert max(errs) < LOGIT_TOL, errs
+
+
+def test_sliding_window_dense(cuda):
+    s = synth.dense_spec("llama", seed=5, layers=2, hidden=256, ffn=512, heads=4, kv_heads=2, head_dim=64, vocab=300,
+                         eps=1e-5, theta=1e4, wtype=synth.Q8_0, std=0.05,
+                         extra=[("llama.attention.sliding_window", synth.T_U32, 7)])
+    s.prompt = synth.uniform_ids(19, 300, seed=5)
+    tokens, ref, errs, margins = compare(s, 5, batch=8)
+    assert tokens == ref, (tokens, ref, margins)
+    assert max(errs) < LOGIT_TOL, errs
+
+
+def test_ungated_mlp_and_output_bias(cuda):
+    s = synth.dense_spec("qwen2", seed=6, layers=2, hidden=128, ffn=256, heads=4, kv_heads=4, head_dim=32, vocab=200,
+                         eps=1e-6, theta=1e6, wtype=synth.F16, bias=True, gate=False, std=0.05)
+    for l in range(2):
+        s.tensors.append(synth.TensorSpec(f"blk.{l}.attn_output.bias", (128,), synth.F32, "normal", 0.05, 900 + l))
+    s.prompt = synth.uniform_ids(9, 200, seed=6)
+    tokens, ref, errs, margins = compare(s, 4, batch=8)
+    assert tokens == ref, (tokens, ref, margins)
+    assert max(errs) < LOGIT_TOL, errs
+
+
+def test_qwen05_architecture_two_layers(cuda):
+    """Full-width Qwen2.5-0.5B layers (Q4_0/Q4_K mix, Q8_0 tied embedding, biases), prefill batch 32."""
+    tokens, ref, errs, margins = compare(synth.baseline_spec(2, layers=2), 4, batch=32)
+    assert tokens == ref, (tokens, ref, margins)
+    assert max(errs) < LOGIT_TOL, errs
+
+
+def test_llama8b_architecture_one_layer(cuda):
+    """Full-width Llama-3-8B layer (Q4_K) with the Q6_K 128256-row head."""
+    s = synth.baseline_spec(3, layers=1)
+    s.prompt = s.prompt[:12]
+    tokens, ref, errs, margins = compare(s, 3, batch=8)
+    assert tokens == ref, (tokens, ref, margins)
+    assert max(errs) < LOGIT_TOL, errs
+
+
+def test_graph_replay_equals_eager(cuda):
+    spec = synth.baseline_spec(0)
+    image = synth.build_gguf(spec)
+    outs = []
+    for graphs in (1, 0):
+        e, _ = load(spec, batch=8, image=image)
+        from webgpu_b200 import _native
+        _native.lib().wgd_set_graphs(e.ctx, graphs)
+        seq = []
+        out = e.forward(spec.prompt, 0, True, want_logits=False)
+        pos = len(spec.prompt)
+        for _ in range(6):
+            seq.append(out)
+            out = e.forward([out], pos, True)
+            pos += 1
+        outs.append(seq)
+        e.dispose()
+    assert outs[0] == outs[1]
+
+
+def test_budget_and_argument_errors(cuda):
+    from webgpu_b200._native import WgdError
+    spec = synth.baseline_spec(3, layers=2)
+    with pytest.raises(WgdError) as ei:
+        load(spec, context=4096, batch=16, budget=1024)
+    assert "GPU budget exceeded" in str(ei.value)
+    e, _ = load(synth.baseline_spec(0), batch=8)
+    with pytest.raises(WgdError, match="token id out of range"):
+        e.forward([600], 0, True)
+    with pytest.raises(WgdError, match="context"):
+        e.forward([1, 2], 511, True)
+    e.dispose()
+
+
+def test_cancel_is_observed_between_forwards(cuda):
+    from webgpu_b200.engine import AbortError
+    e, _ = load(synth.baseline_spec(0), batch=8)
+    e.cancel()
+    with pytest.raises(AbortError):
+        e.forward([1], 0, True)
+    assert e.forward([1], 0, True) >= 0
+    e.dispose()

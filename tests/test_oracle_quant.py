@@ -136,3 +136,16 @@ def test_f32_twin_within_one_ulp_of_f64(ttype):
     finite = np.isfinite(f64)
     ulp = np.spacing(np.abs(f64[finite]).astype(np.float32)).astype(np.float64)
     assert np.all(np.abs(f32[finite] - f64[finite]) <= ulp + 1e-45)
+
+
+@pytest.mark.parametrize("ttype", [0, 1, 2, 8, 12, 13, 14])
+def test_hoisted_row_decoder_is_bit_identical(ttype):
+    """The oracle's fast row decoder equals the literal decodeWeight restatement bitwise."""
+    import ctypes
+    L = oracle.lib()
+    L.or_dequant_row_matches.restype = ctypes.c_int
+    L.or_dequant_row_matches.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64]
+    cols = 2048
+    be = synth.BLOCK[ttype][0]
+    raw = synth.random_blocks(ttype, cols // be, seed=21, stream=ttype)
+    assert L.or_dequant_row_matches(ctypes.c_void_p(raw.ctypes.data), ttype, cols) == 1

@@ -60,6 +60,8 @@ SIGNATURES = {
     "wgd_model_ready": (c_int, [c_void_p, ctypes.POINTER(c_int)]),
     "wgd_model_placement": (c_int, [c_void_p, ctypes.POINTER(c_uint64), ctypes.POINTER(c_uint64)]),
     "wgd_forward": (c_int, [c_void_p, ctypes.POINTER(c_int32), c_int, c_int, c_int, ctypes.POINTER(c_int32), ctypes.POINTER(c_float)]),
+    "wgd_decode": (c_int, [c_void_p, c_int32, c_int, c_int, ctypes.POINTER(c_int32)]),
+    "wgd_kernels_per_token": (c_int, [c_void_p, ctypes.POINTER(c_int)]),
     "wgd_truncate_kv": (c_int, [c_void_p, c_int]),
     "wgd_cancel": (None, [c_void_p]),
     "wgd_stats_get": (c_int, [c_void_p, ctypes.POINTER(StatsC)]),
@@ -68,6 +70,10 @@ SIGNATURES = {
     "wgd_op_repack": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "wgd_op_dequant": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "wgd_op_gemv": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "wgd_tiled_bytes": (c_int64, [c_int, c_int64, c_int64]),
+    "wgd_op_repack_tiled": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
+    "wgd_op_dequant_tiled": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
+    "wgd_op_gemv_tiled": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "wgd_op_rmsnorm": (c_int, [c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_void_p]),
     "wgd_op_rope": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_float, c_float, c_int, c_int, c_void_p]),
     "wgd_op_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_int,

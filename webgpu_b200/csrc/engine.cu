@@ -25,6 +25,7 @@
 #include "../../include/wgd.h"
 #include "common.cuh"
 #include "kernels.h"
+#include "tile.cuh"
 #include "tp.h"
 
 using namespace wgd;
@@ -44,8 +45,10 @@ namespace {
 
 struct DevLinear {
   int type = -1, rows = 0, cols = 0, nb = 0;
-  int64_t drow = 0;
+  int64_t drow = 0;    // row layout: bytes per row
+  bool tiled = false;  // tile-16 layout (tensor-core GEMV)
   uint8_t *w = nullptr;
+  int64_t bytes() const { return tiled ? tiled_bytes(type, rows, cols) : drow * rows; }
 };
 
 enum Role {
@@ -119,11 +122,17 @@ struct wgd_ctx {
   int att_splits = 1, gemv_slot = 0;
   uint8_t *staging = nullptr;
   size_t staging_bytes = 0;
+  float *g2_part = nullptr;  // stream-K partials of the tensor-core GEMV
+  size_t g2_part_floats = 0;
+  unsigned *g2_ctr = nullptr;
+  int g2_ctr_count = 0;
   int32_t *h_io = nullptr;  // pinned: [0] start, [1] argmax, [2..] ids
   // graph
   bool graphs = true;
-  cudaGraphExec_t decode_exec = nullptr;
-  cudaGraph_t decode_graph = nullptr;
+  cudaGraphExec_t decode_exec = nullptr, chain_exec = nullptr;
+  cudaGraph_t decode_graph = nullptr, chain_graph = nullptr;
+  int *d_tokens = nullptr, *d_step = nullptr;
+  int kernels = 0;  // kernels launched by the last enqueued forward
   std::atomic<int> cancel{0};
   wgd_stats st{};
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -158,8 +167,10 @@ static int ctx_alloc_t(wgd_ctx *ctx, T **p, size_t count, const char *label) {
 static void free_all(wgd_ctx *ctx) {
   if (ctx->decode_exec) cudaGraphExecDestroy(ctx->decode_exec);
   if (ctx->decode_graph) cudaGraphDestroy(ctx->decode_graph);
-  ctx->decode_exec = nullptr;
-  ctx->decode_graph = nullptr;
+  if (ctx->chain_exec) cudaGraphExecDestroy(ctx->chain_exec);
+  if (ctx->chain_graph) cudaGraphDestroy(ctx->chain_graph);
+  ctx->decode_exec = ctx->chain_exec = nullptr;
+  ctx->decode_graph = ctx->chain_graph = nullptr;
   for (auto &a : ctx->allocs) cudaFree(a.p);
   ctx->allocs.clear();
   ctx->allocated = 0;
@@ -331,15 +342,21 @@ static int alloc_linear(wgd_ctx *ctx, DevLinear &L, int type, int rows, int cols
   L.cols = cols;
   L.nb = cols / block_elems(type);
   L.drow = dev_row_bytes(type, cols);
+  L.tiled = tiled_type(type) && gemv2_max_batch(cols) > 0;
   if (cols % 32) return fail(WGD_EINVAL, std::string("matrix width must be a multiple of 32: ") + label);
-  if (gemv_max_batch(cols) == 0) return fail(WGD_EINVAL, std::string("matrix too wide for the GEMV kernel: ") + label);
-  return ctx_alloc_t(ctx, &L.w, (size_t)L.drow * rows + 16, label);
+  if (!L.tiled && gemv_max_batch(cols) == 0) return fail(WGD_EINVAL, std::string("matrix too wide for the GEMV kernel: ") + label);
+  if (L.tiled) {
+    const size_t pf = gemv2_part_floats(type, rows, cols, ctx->sm_count);
+    if (pf > ctx->g2_part_floats) ctx->g2_part_floats = pf;
+    if ((rows + 15) / 16 > ctx->g2_ctr_count) ctx->g2_ctr_count = (rows + 15) / 16;
+  }
+  return ctx_alloc_t(ctx, &L.w, (size_t)L.bytes() + 16, label);
 }
 
 // A matrix part: GGUF rows [src_begin, src_end) -> device rows (map), columns [blk0, blk0+nbl) in blocks.
 static void place(TensorRec *t, DevLinear *L, int src_begin, int src_end, int dst_base, int interleave, int blk0, int nbl) {
   t->lin = L;
-  t->map = RowMap{src_begin, src_end, dst_base, interleave, 0};
+  t->map = RowMap{src_begin, src_end, dst_base, interleave, L->tiled ? TILE_ROWS / 2 : GEMV_ROWS / 2};
   t->blk0 = blk0;
   t->nbl = nbl;
 }
@@ -383,8 +400,10 @@ extern "C" int wgd_model_end(wgd_ctx *ctx) {
   ctx->ffn0 = part_begin(fblocks, r, tp) * funit;
   ctx->ffn_l = part_begin(fblocks, r + 1, tp) * funit - ctx->ffn0;
   if (ctx->ffn_l % 2) return fail(WGD_EINVAL, "feed-forward shard must have an even row count");
-  ctx->vocab0 = part_begin(c.vocab, r, tp);
-  ctx->vocab_l = part_begin(c.vocab, r + 1, tp) - ctx->vocab0;
+  // vocabulary rows split in whole 16-row tiles
+  const int vt = (c.vocab + 15) / 16;
+  ctx->vocab0 = std::min(c.vocab, part_begin(vt, r, tp) * 16);
+  ctx->vocab_l = std::min(c.vocab, part_begin(vt, r + 1, tp) * 16) - ctx->vocab0;
 
   ctx->layers.assign(c.layers, Layer());
   const int B = ctx->max_batch;
@@ -491,7 +510,8 @@ extern "C" int wgd_model_end(wgd_ctx *ctx) {
   place(embd, &ctx->embd, 0, c.vocab, 0, 0, 0, ctx->embd.nb);
   if (ctx->tied) {
     ctx->lm = ctx->embd;
-    ctx->lm.w = ctx->embd.w + (int64_t)ctx->vocab0 * ctx->embd.drow;
+    ctx->lm.w = ctx->embd.w + (ctx->embd.tiled ? (int64_t)(ctx->vocab0 / 16) * ctx->embd.nb * tile_chunk_bytes(embd->type)
+                                               : (int64_t)ctx->vocab0 * ctx->embd.drow);
     ctx->lm.rows = ctx->vocab_l;
   } else {
     if ((rc = alloc_linear(ctx, ctx->lm, output->type, ctx->vocab_l, H, "output"))) return rc;
@@ -507,7 +527,8 @@ extern "C" int wgd_model_end(wgd_ctx *ctx) {
       (rc = ctx_alloc_t(ctx, &ctx->proj, (size_t)B * H, "projection")) || (rc = ctx_alloc_t(ctx, &ctx->act, (size_t)B * F, "ffn")) ||
       (rc = ctx_alloc_t(ctx, &ctx->logits, (size_t)c.vocab, "logits")) || (rc = ctx_alloc_t(ctx, &ctx->d_ids, (size_t)B, "ids")) ||
       (rc = ctx_alloc_t(ctx, &ctx->d_start, 4, "start")) || (rc = ctx_alloc_t(ctx, &ctx->d_argmax, 4, "argmax")) ||
-      (rc = ctx_alloc_t(ctx, &ctx->d_err, 4, "err")) || (rc = ctx_alloc_t(ctx, &ctx->d_maxval, 4, "maxval")))
+      (rc = ctx_alloc_t(ctx, &ctx->d_err, 4, "err")) || (rc = ctx_alloc_t(ctx, &ctx->d_maxval, 4, "maxval")) ||
+      (rc = ctx_alloc_t(ctx, &ctx->d_tokens, (size_t)ctx->context, "decoded tokens")) || (rc = ctx_alloc_t(ctx, &ctx->d_step, 4, "step")))
     return rc;
   ctx->att_splits = attention_splits(ctx->context);
   if ((rc = ctx_alloc_t(ctx, &ctx->att_part, attention_part_floats(B, c.heads / tp, ctx->kv_l, hd, ctx->att_splits), "attention partials")))
@@ -518,6 +539,9 @@ extern "C" int wgd_model_end(wgd_ctx *ctx) {
     return rc;
   ctx->staging_bytes = 64u << 20;
   if ((rc = ctx_alloc_t(ctx, &ctx->staging, ctx->staging_bytes, "upload staging"))) return rc;
+  if (ctx->g2_part_floats && ((rc = ctx_alloc_t(ctx, &ctx->g2_part, ctx->g2_part_floats, "gemv partials")) ||
+                              (rc = ctx_alloc_t(ctx, &ctx->g2_ctr, (size_t)ctx->g2_ctr_count, "gemv tile counters"))))
+    return rc;
   if (tp > 1) {
     if ((rc = tp_create(&ctx->tp, ctx->tp_rank, tp, (size_t)B * H, &g_err))) return rc;
   }
@@ -568,8 +592,12 @@ extern "C" int wgd_tensor_upload(wgd_ctx *ctx, const char *name, uint64_t byte_o
     const int64_t cnt = std::min(chunk_rows, keep1 - a);
     const uint8_t *src = (const uint8_t *)host + (a - row0) * t->row_bytes;
     CK(cudaMemcpyAsync(ctx->staging, src, cnt * t->row_bytes, cudaMemcpyHostToDevice, ctx->stream));
-    CK(launch_repack(t->type, ctx->staging, (int64_t)t->row_bytes, (int)a, (int)cnt, t->blk0, t->nbl, t->lin->w, t->lin->drow,
-                     t->map, ctx->stream));
+    if (t->lin->tiled)
+      CK(launch_repack_tiled(t->type, ctx->staging, (int64_t)t->row_bytes, (int)a, (int)cnt, t->blk0, t->nbl, t->lin->w,
+                             t->lin->rows, t->map, ctx->stream));
+    else
+      CK(launch_repack(t->type, ctx->staging, (int64_t)t->row_bytes, (int)a, (int)cnt, t->blk0, t->nbl, t->lin->w, t->lin->drow,
+                       t->map, ctx->stream));
     CK(cudaStreamSynchronize(ctx->stream));
   }
   t->uploaded_rows += nrows;
@@ -611,8 +639,8 @@ extern "C" int wgd_model_ready(wgd_ctx *ctx, int *ready) {
 extern "C" int wgd_model_placement(wgd_ctx *ctx, uint64_t *resident, uint64_t *streamed) {
   if (!ctx) return fail(WGD_EINVAL, "null context");
   uint64_t res = 0;
-  for (auto &L : ctx->layers) res += L.qkv.drow * L.qkv.rows + L.o.drow * L.o.rows + L.gate_up.drow * L.gate_up.rows + L.down.drow * L.down.rows;
-  res += ctx->embd.drow * ctx->embd.rows + (ctx->tied ? 0 : ctx->lm.drow * ctx->lm.rows);
+  for (auto &L : ctx->layers) res += L.qkv.bytes() + L.o.bytes() + L.gate_up.bytes() + L.down.bytes();
+  res += ctx->embd.bytes() + (ctx->tied ? 0 : ctx->lm.bytes());
   if (resident) *resident = res;
   if (streamed) *streamed = 0;
   return WGD_OK;
@@ -622,6 +650,29 @@ extern "C" int wgd_model_placement(wgd_ctx *ctx, uint64_t *resident, uint64_t *s
 
 static int gemv(wgd_ctx *ctx, const DevLinear &L, const float *x, int ldx, const float *norm_w, float *y, int ldy,
                 const float *bias, int epi, int batch) {
+  const int chunk = L.tiled ? gemv2_max_batch(L.cols) : gemv_max_batch(L.cols);
+  ctx->kernels += chunk > 0 ? (batch + chunk - 1) / chunk : 1;
+  if (L.tiled) {
+    Gemv2Launch g{};
+    g.w = L.w;
+    g.rows = L.rows;
+    g.cols = L.cols;
+    g.x = x;
+    g.ldx = ldx;
+    g.norm_w = norm_w;
+    g.eps = ctx->c.epsilon;
+    g.y = y;
+    g.ldy = ldy;
+    g.bias = bias;
+    g.epi = epi;
+    g.batch = batch;
+    g.part = ctx->g2_part;
+    g.part_floats = ctx->g2_part_floats;
+    g.tile_ctr = ctx->g2_ctr;
+    g.ctr_count = ctx->g2_ctr_count;
+    CK(launch_gemv2(L.type, g, ctx->stream, true, ctx->sm_count));
+    return WGD_OK;
+  }
   GemvArgs a{};
   a.w = L.w;
   a.drow = L.drow;
@@ -649,16 +700,21 @@ static int tp_reduce_add(wgd_ctx *ctx, const float *partial, float *hidden, int 
 }
 
 // Enqueues one forward of n rows (positions from *d_start) on ctx->stream.
-static int enqueue_forward(wgd_ctx *ctx, int n, bool want_logits_rows) {
+// io: copy ids/start in from pinned host memory and the argmax out again.
+static int enqueue_forward(wgd_ctx *ctx, int n, bool want_logits_rows, bool io = true) {
   const wgd_model_config &c = ctx->c;
   const int H = c.hidden, hd = c.head_dim;
   const bool gemma = c.family == 1, tp1 = ctx->tp_size == 1;
   int rc;
   ctx->gemv_slot = 0;
-  CK(cudaMemcpyAsync(ctx->d_start, ctx->h_io, sizeof(int32_t), cudaMemcpyHostToDevice, ctx->stream));
-  CK(cudaMemcpyAsync(ctx->d_ids, ctx->h_io + 2, sizeof(int32_t) * n, cudaMemcpyHostToDevice, ctx->stream));
+  ctx->kernels = 0;
+  if (io) {
+    CK(cudaMemcpyAsync(ctx->d_start, ctx->h_io, sizeof(int32_t), cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(ctx->d_ids, ctx->h_io + 2, sizeof(int32_t) * n, cudaMemcpyHostToDevice, ctx->stream));
+  }
+  ctx->kernels += 1 + c.layers * 2 + 1 + (gemma ? 2 * c.layers : 0) + (tp1 ? 0 : (gemma ? 2 : 2) * c.layers + 1);
   CK(launch_embed(ctx->embd.type, ctx->embd.w, ctx->embd.drow, H, ctx->d_ids, n, c.vocab, gemma ? sqrtf((float)H) : 1.f,
-                  ctx->hidden, H, ctx->d_err, ctx->stream, false));
+                  ctx->hidden, H, ctx->d_err, ctx->stream, false, ctx->embd.tiled));
   for (int l = 0; l < c.layers; l++) {
     Layer &L = ctx->layers[l];
     if ((rc = gemv(ctx, L.qkv, ctx->hidden, H, L.attn_norm, ctx->qkv, ctx->qkv_rows, L.qkv_bias, EPI_STORE, n))) return rc;
@@ -735,7 +791,7 @@ static int enqueue_forward(wgd_ctx *ctx, int n, bool want_logits_rows) {
         (rc = tp_gather_rows(ctx->tp, ctx->logits, ctx->c.vocab, ctx->vocab0, ctx->vocab_l, ctx->stream, ctx->tp_spin_limit, &g_err)))
       return rc;
   }
-  CK(cudaMemcpyAsync(ctx->h_io + 1, ctx->d_argmax, sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream));
+  if (io) CK(cudaMemcpyAsync(ctx->h_io + 1, ctx->d_argmax, sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream));
   return WGD_OK;
 }
 
@@ -786,6 +842,62 @@ extern "C" int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, i
     if (ctx->h_io[1] < 0) return fail(WGD_ENONFINITE, "Inference produced non-finite logits. Stop and report this model/runtime combination.");
     if (argmax_out) *argmax_out = ctx->h_io[1];
   }
+  return WGD_OK;
+}
+
+extern "C" int wgd_decode(wgd_ctx *ctx, int32_t first, int start, int steps, int32_t *tokens_out) {
+  if (!ctx || !tokens_out) return fail(WGD_EINVAL, "null argument");
+  if (!ctx->ended) return fail(WGD_ESTATE, "Load a model first.");
+  std::string missing;
+  if (!all_uploaded(ctx, &missing)) return fail(WGD_ESTATE, "weights not uploaded: " + missing);
+  if (steps < 1 || start < 0 || start + steps > ctx->context) return fail(WGD_EINVAL, "positions exceed the context length");
+  if (first < 0 || first >= ctx->c.vocab) return fail(WGD_EINVAL, "token id out of range");
+  if (ctx->cancel.exchange(0)) return fail(WGD_ECANCELLED, "Stopped by user");
+  CK(cudaSetDevice(ctx->device));
+  int rc;
+  if (!ctx->chain_exec) {
+    CK(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+    rc = enqueue_forward(ctx, 1, false, false);
+    if (!rc) {
+      cudaError_t e = launch_advance(ctx->d_ids, ctx->d_start, ctx->d_argmax, ctx->d_tokens, ctx->d_step, ctx->d_err, ctx->stream, true);
+      if (e != cudaSuccess) rc = fail(WGD_ECUDA, std::string("advance: ") + cudaGetErrorString(e));
+      ctx->kernels += 1;
+    }
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+    if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+    if (e != cudaSuccess) return fail(WGD_ECUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    ctx->chain_graph = g;
+    CK(cudaGraphInstantiate(&ctx->chain_exec, g, 0));
+  }
+  ctx->h_io[0] = start;
+  ctx->h_io[2] = first;
+  ctx->h_io[3] = 0;
+  CK(cudaMemcpyAsync(ctx->d_start, ctx->h_io, sizeof(int32_t), cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaMemcpyAsync(ctx->d_ids, ctx->h_io + 2, sizeof(int32_t), cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaMemcpyAsync(ctx->d_step, ctx->h_io + 3, sizeof(int32_t), cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaMemsetAsync(ctx->d_err, 0, sizeof(int32_t), ctx->stream));
+  CK(cudaEventRecord(ctx->ev0, ctx->stream));
+  for (int i = 0; i < steps; i++) CK(cudaGraphLaunch(ctx->chain_exec, ctx->stream));
+  CK(cudaEventRecord(ctx->ev1, ctx->stream));
+  CK(cudaMemcpyAsync(tokens_out, ctx->d_tokens, sizeof(int32_t) * steps, cudaMemcpyDeviceToHost, ctx->stream));
+  int32_t err = 0;
+  CK(cudaMemcpyAsync(&err, ctx->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream));
+  CK(cudaStreamSynchronize(ctx->stream));
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, ctx->ev0, ctx->ev1);
+  ctx->st.last_forward_ms = ms;
+  ctx->st.forwards += steps;
+  ctx->st.tokens += steps;
+  if (ctx->tp && tp_failed(ctx->tp)) return fail(WGD_ETIMEOUT, "a tensor-parallel peer did not answer within the wait limit");
+  if (err == 2) return fail(WGD_ENONFINITE, "Inference produced non-finite logits. Stop and report this model/runtime combination.");
+  return WGD_OK;
+}
+
+extern "C" int wgd_kernels_per_token(wgd_ctx *ctx, int *count) {
+  if (!ctx || !count) return fail(WGD_EINVAL, "null argument");
+  if (!ctx->ended) return fail(WGD_ESTATE, "Load a model first.");
+  *count = ctx->kernels;
   return WGD_OK;
 }
 
@@ -984,5 +1096,77 @@ extern "C" int wgd_op_argmax(const float *x, int n, int32_t *idx, void *stream) 
   float *part;
   if ((rc = op_part(2 * 256 + 4, &part))) return rc;
   CK(launch_argmax(x, n, idx, nullptr, part, ctr + 4000, (cudaStream_t)stream, false));
+  return WGD_OK;
+}
+
+// ------------------------------------------------------------ tiled-layout ops
+
+namespace {
+float *g_t_part[16] = {nullptr};
+size_t g_t_part_n[16] = {0};
+unsigned *g_t_ctr[16] = {nullptr};
+int g_t_ctr_n[16] = {0};
+}  // namespace
+
+extern "C" int64_t wgd_tiled_bytes(int type, int64_t rows, int64_t cols) {
+  if (!tiled_type(type) || cols % 256 || rows < 1) return -1;
+  return tiled_bytes(type, rows, cols);
+}
+
+extern "C" int wgd_op_repack_tiled(int type, int64_t rows, int64_t cols, const void *raw, void *tiled, void *stream) {
+  if (!tiled_type(type) || cols % 256 || rows < 1) return fail(WGD_EINVAL, "tiled layout needs Q4_K/Q6_K and whole super-blocks");
+  RowMap m{0, (int)rows, 0, 0, TILE_ROWS / 2};
+  CK(launch_repack_tiled(type, (const uint8_t *)raw, gguf_row_bytes(type, cols), 0, (int)rows, 0, (int)(cols / 256),
+                         (uint8_t *)tiled, (int)rows, m, (cudaStream_t)stream));
+  return WGD_OK;
+}
+
+extern "C" int wgd_op_dequant_tiled(int type, int64_t rows, int64_t cols, const void *tiled, float *out, void *stream) {
+  if (!tiled_type(type) || cols % 256) return fail(WGD_EINVAL, "tiled layout needs Q4_K/Q6_K and whole super-blocks");
+  CK(launch_dequant_tiled(type, (const uint8_t *)tiled, (int)rows, (int)cols, out, cols, (cudaStream_t)stream));
+  return WGD_OK;
+}
+
+extern "C" int wgd_op_gemv_tiled(int type, int64_t rows, int64_t cols, const void *tiled, const float *x, int batch, float *y,
+                                 void *stream) {
+  if (!tiled_type(type) || cols % 256 || rows < 1 || batch < 1 || gemv2_max_batch((int)cols) == 0)
+    return fail(WGD_EINVAL, "bad type, shape or batch for the tiled GEMV");
+  int dev = 0, sm = 0;
+  unsigned *unused;
+  int rc;
+  if ((rc = op_scratch(&unused, &sm))) return rc;  // caches the SM count of this device
+  CK(cudaGetDevice(&dev));
+  const size_t need = gemv2_part_floats(type, (int)rows, (int)cols, sm);
+  const int tiles = (int)((rows + 15) / 16);
+  {
+    std::lock_guard<std::mutex> lk(g_op_mu);
+    if (g_t_part_n[dev] < need) {
+      if (g_t_part[dev]) cudaFree(g_t_part[dev]);
+      CK(cudaMalloc(&g_t_part[dev], need * sizeof(float)));
+      g_t_part_n[dev] = need;
+    }
+    if (g_t_ctr_n[dev] < tiles) {
+      if (g_t_ctr[dev]) cudaFree(g_t_ctr[dev]);
+      CK(cudaMalloc(&g_t_ctr[dev], tiles * sizeof(unsigned)));
+      CK(cudaMemset(g_t_ctr[dev], 0, tiles * sizeof(unsigned)));
+      g_t_ctr_n[dev] = tiles;
+    }
+  }
+  Gemv2Launch g{};
+  g.w = (const uint8_t *)tiled;
+  g.rows = (int)rows;
+  g.cols = (int)cols;
+  g.x = x;
+  g.ldx = (int)cols;
+  g.eps = 0.f;
+  g.y = y;
+  g.ldy = (int)rows;
+  g.epi = EPI_STORE;
+  g.batch = batch;
+  g.part = g_t_part[dev];
+  g.part_floats = g_t_part_n[dev];
+  g.tile_ctr = g_t_ctr[dev];
+  g.ctr_count = g_t_ctr_n[dev];
+  CK(launch_gemv2(type, g, (cudaStream_t)stream, false, sm));
   return WGD_OK;
 }

@@ -39,6 +39,33 @@ cudaError_t launch_gemv(int type, const GemvArgs &a, cudaStream_t s, bool pdl, i
 // Largest batch chunk the register-resident GEMV handles for this width in one pass.
 int gemv_max_batch(int cols);
 
+// ------------------------------------------------------- tensor-core GEMV
+// Same operation over the tile-16 layout (tile.cuh) for Q4_K / Q6_K weights.
+// `part`/`tile_ctr` are stream-K scratch: part_floats >= gemv2_part_floats(...),
+// tile_ctr holds >= tiles zeroed counters (left zeroed).
+struct Gemv2Launch {
+  const uint8_t *w;
+  int rows, cols;
+  const float *x;
+  int ldx;
+  const float *norm_w;
+  float eps;
+  float *y;
+  int ldy;
+  const float *bias;
+  int epi;
+  int batch;
+  float *part;
+  size_t part_floats;
+  unsigned *tile_ctr;
+  int ctr_count;
+};
+cudaError_t launch_gemv2(int type, const Gemv2Launch &a, cudaStream_t s, bool pdl, int sm_count);
+// Upper bound of the partial-sum floats one launch may need.
+size_t gemv2_part_floats(int type, int rows, int cols, int sm_count);
+// Largest activation chunk per pass (0 if the width is unsupported).
+int gemv2_max_batch(int cols);
+
 // --------------------------------------------------------------- layout
 // Raw GGUF rows -> device rows. Source rows [0, nrows) at `src` (row stride
 // `src_row_bytes`); block columns [blk0, blk0 + nbl) of each row are moved to
@@ -47,16 +74,20 @@ struct RowMap {
   int src_begin;   // first source row kept (global row index)
   int src_end;     // one past the last kept row
   int dst_base;    // logical destination row of src_begin
-  int interleave;  // 0: plain; 1: gate part; 2: up part (GLU interleave of 2)
-  int glu_rows;    // logical rows of one GLU part (for interleave)
+  int interleave;  // 0: plain; 1: gate part; 2: up part (GLU interleave)
+  int glu_block;   // GLU interleave block R: device rows [R gate][R up] repeat
 };
 cudaError_t launch_repack(int type, const uint8_t *src, int64_t src_row_bytes, int row0, int nrows, int blk0, int nbl,
                           uint8_t *dst, int64_t dst_row_bytes, RowMap map, cudaStream_t s);
 cudaError_t launch_dequant(int type, const uint8_t *w, int64_t drow, int rows, int cols, float *out, int64_t ldo,
                            cudaStream_t s);
+// Tiled layout: same meaning; destination rows are placed in tiles of 16.
+cudaError_t launch_repack_tiled(int type, const uint8_t *src, int64_t src_row_bytes, int row0, int nrows, int blk0, int nbl,
+                                uint8_t *dst, int dst_rows, RowMap map, cudaStream_t s);
+cudaError_t launch_dequant_tiled(int type, const uint8_t *w, int rows, int cols, float *out, int64_t ldo, cudaStream_t s);
 // Dequantises selected rows (ids[t]) scaled by `scale` into out[t][cols] (embedding gather).
 cudaError_t launch_embed(int type, const uint8_t *w, int64_t drow, int cols, const int *ids, int n, int vocab, float scale,
-                         float *out, int ldo, int *err, cudaStream_t s, bool pdl);
+                         float *out, int ldo, int *err, cudaStream_t s, bool pdl, bool tiled = false);
 
 // ---------------------------------------------------------- block ops
 // RMS norm of x rows (n rows of `cols`) with weight w: y = x * rsqrt(mean(x^2)+eps) * w.
@@ -103,6 +134,10 @@ size_t attention_part_floats(int n, int heads, int kv_heads, int hd, int splits)
 cudaError_t launch_argmax(const float *x, int n, int *out_idx, float *out_val, float *part, unsigned *ctr, cudaStream_t s,
                           bool pdl);
 int argmax_blocks(int n);
+
+// Device decode loop step: ids[0] = *argmax; *start += 1; tokens[*step] = *argmax; ++*step.
+// A non-finite row (argmax -1) sets *err and feeds token 0.
+cudaError_t launch_advance(int *ids, int *start, const int *argmax, int *tokens, int *step, int *err, cudaStream_t s, bool pdl);
 
 // Elementwise: y += x (n floats).
 cudaError_t launch_add(const float *x, float *y, int64_t n, cudaStream_t s, bool pdl);

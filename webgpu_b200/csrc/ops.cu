@@ -7,6 +7,7 @@
 #include <float.h>
 #include "kernels.h"
 #include "quant.cuh"
+#include "tile.cuh"
 
 namespace wgd {
 
@@ -15,7 +16,8 @@ namespace wgd {
 __device__ __forceinline__ int map_row(const RowMap &m, int grow) {
   int i = grow - m.src_begin;
   if (m.interleave == 0) return m.dst_base + i;
-  return (i >> 1) * 4 + (m.interleave == 2 ? 2 : 0) + (i & 1);
+  const int R = m.glu_block;
+  return (i / R) * 2 * R + (m.interleave == 2 ? R : 0) + (i % R);
 }
 
 __global__ void repack_kernel(int type, const uint8_t *src, int64_t srb, int row0, int nrows, int blk0, int nbl, uint8_t *dst,
@@ -37,6 +39,48 @@ cudaError_t launch_repack(int type, const uint8_t *src, int64_t src_row_bytes, i
   int threads = 256;
   int64_t blocks = (total + threads - 1) / threads;
   repack_kernel<<<(unsigned)blocks, threads, 0, s>>>(type, src, src_row_bytes, row0, nrows, blk0, nbl, dst, dst_row_bytes, map);
+  return cudaGetLastError();
+}
+
+__global__ void repack_tiled_kernel(int type, const uint8_t *src, int64_t srb, int row0, int nrows, int blk0, int nbl, uint8_t *dst,
+                                    RowMap m) {
+  const int bb = type == Q4_K ? 144 : 210;
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)nrows * nbl) return;
+  int r = (int)(idx / nbl), bi = (int)(idx % nbl);
+  int grow = row0 + r;
+  if (grow < m.src_begin || grow >= m.src_end) return;
+  const int drow = map_row(m, grow), t = drow >> 4, lr = drow & 15;
+  const uint8_t *s = src + (int64_t)r * srb + (int64_t)(blk0 + bi) * bb;
+  uint8_t *chunk = dst + ((int64_t)t * nbl + bi) * (16 * bb);
+  for (int b = 0; b < bb; b++) chunk[tile_offset(type, lr, b)] = s[b];
+}
+
+cudaError_t launch_repack_tiled(int type, const uint8_t *src, int64_t src_row_bytes, int row0, int nrows, int blk0, int nbl,
+                                uint8_t *dst, int dst_rows, RowMap map, cudaStream_t s) {
+  (void)dst_rows;
+  if (!tiled_type(type)) return cudaErrorInvalidValue;
+  int64_t total = (int64_t)nrows * nbl;
+  if (total == 0) return cudaSuccess;
+  repack_tiled_kernel<<<(unsigned)((total + 127) / 128), 128, 0, s>>>(type, src, src_row_bytes, row0, nrows, blk0, nbl, dst, map);
+  return cudaGetLastError();
+}
+
+template <int T>
+__global__ void dequant_tiled_kernel(const uint8_t *w, int rows, int cols, float *out, int64_t ldo) {
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)rows * cols) return;
+  int r = (int)(idx / cols), c = (int)(idx % cols);
+  out[(int64_t)r * ldo + c] = dequant_tiled<T>(w, cols / 256, r, c);
+}
+
+cudaError_t launch_dequant_tiled(int type, const uint8_t *w, int rows, int cols, float *out, int64_t ldo, cudaStream_t s) {
+  int64_t total = (int64_t)rows * cols;
+  if (total == 0) return cudaSuccess;
+  const unsigned blocks = (unsigned)((total + 255) / 256);
+  if (type == Q4_K) dequant_tiled_kernel<Q4_K><<<blocks, 256, 0, s>>>(w, rows, cols, out, ldo);
+  else if (type == Q6_K) dequant_tiled_kernel<Q6_K><<<blocks, 256, 0, s>>>(w, rows, cols, out, ldo);
+  else return cudaErrorInvalidValue;
   return cudaGetLastError();
 }
 
@@ -88,13 +132,30 @@ __global__ void embed_kernel(const uint8_t *w, int64_t drow, int cols, const int
 }
 
 template <int T>
+__global__ void embed_tiled_kernel(const uint8_t *w, int cols, const int *ids, int vocab, float scale, float *out, int ldo, int *err) {
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int id = ids[t];
+  const bool ok = id >= 0 && id < vocab;
+  if (!ok && threadIdx.x == 0 && err) *err = 1;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x)
+    out[(int64_t)t * ldo + c] = ok ? dequant_tiled<T>(w, cols / 256, id, c) * scale : 0.f;
+  pdl_launch_dependents();
+}
+
+template <int T>
 static cudaError_t emb(const uint8_t *w, int64_t drow, int cols, const int *ids, int n, int vocab, float scale, float *out,
                        int ldo, int *err, cudaStream_t s, bool pdl) {
   return launch_k(embed_kernel<T>, dim3(n), dim3(256), 0, s, pdl, w, drow, cols, ids, vocab, scale, out, ldo, err);
 }
 
 cudaError_t launch_embed(int type, const uint8_t *w, int64_t drow, int cols, const int *ids, int n, int vocab, float scale,
-                         float *out, int ldo, int *err, cudaStream_t s, bool pdl) {
+                         float *out, int ldo, int *err, cudaStream_t s, bool pdl, bool tiled) {
+  if (tiled) {
+    if (type == Q4_K) return launch_k(embed_tiled_kernel<Q4_K>, dim3(n), dim3(256), 0, s, pdl, w, cols, ids, vocab, scale, out, ldo, err);
+    if (type == Q6_K) return launch_k(embed_tiled_kernel<Q6_K>, dim3(n), dim3(256), 0, s, pdl, w, cols, ids, vocab, scale, out, ldo, err);
+    return cudaErrorInvalidValue;
+  }
   switch (type) {
     case F32: return emb<F32>(w, drow, cols, ids, n, vocab, scale, out, ldo, err, s, pdl);
     case F16: return emb<F16>(w, drow, cols, ids, n, vocab, scale, out, ldo, err, s, pdl);
@@ -456,6 +517,22 @@ __global__ void argmax_kernel(const float *x, int n, int *out_idx, float *out_va
 cudaError_t launch_argmax(const float *x, int n, int *out_idx, float *out_val, float *part, unsigned *ctr, cudaStream_t s,
                           bool pdl) {
   return launch_k(argmax_kernel, dim3(argmax_blocks(n)), dim3(AM_THREADS), 0, s, pdl, x, n, out_idx, out_val, part, ctr);
+}
+
+// ------------------------------------------------------------------ advance
+
+__global__ void advance_kernel(int *ids, int *start, const int *argmax, int *tokens, int *step, int *err) {
+  pdl_wait();
+  const int tok = *argmax;
+  if (tok < 0) *err = 2;
+  ids[0] = tok < 0 ? 0 : tok;
+  *start += 1;
+  tokens[*step] = tok;
+  *step += 1;
+  pdl_launch_dependents();
+}
+cudaError_t launch_advance(int *ids, int *start, const int *argmax, int *tokens, int *step, int *err, cudaStream_t s, bool pdl) {
+  return launch_k(advance_kernel, dim3(1), dim3(1), 0, s, pdl, ids, start, argmax, tokens, step, err);
 }
 
 // ------------------------------------------------------------------ add
