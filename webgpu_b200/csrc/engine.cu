@@ -91,6 +91,7 @@ struct Layer {
   int capacity = 0, window = 0;
   bool local = false;
   double theta = 0, rope_scale = 1;
+  const float2 *rope_table = nullptr;  // (cos, sin)[context][rot/2] for this layer's theta/scale
 };
 
 struct Alloc { void *p; size_t n; };
@@ -122,6 +123,7 @@ struct wgd_ctx {
   int att_splits = 1, gemv_slot = 0;
   uint8_t *staging = nullptr;
   size_t staging_bytes = 0;
+  std::vector<std::pair<std::pair<double, double>, float2 *>> rope_tables;  // (theta, scale) -> table
   float *g2_part = nullptr;  // stream-K partials of the tensor-core GEMV
   size_t g2_part_floats = 0;
   unsigned *g2_ctr = nullptr;
@@ -539,6 +541,31 @@ extern "C" int wgd_model_end(wgd_ctx *ctx) {
     return rc;
   ctx->staging_bytes = 64u << 20;
   if ((rc = ctx_alloc_t(ctx, &ctx->staging, ctx->staging_bytes, "upload staging"))) return rc;
+  // RoPE (cos, sin) tables, one per distinct (theta, scale): angle = pos * scale / theta^(2i/rot),
+  // evaluated in double and rounded once to float (the rope kernels read them)
+  {
+    const int rot = gemma ? hd : (c.rotary_dim ? c.rotary_dim : hd), half = rot / 2;
+    std::vector<float2> host((size_t)ctx->context * half);
+    for (auto &L : ctx->layers) {
+      const auto key = std::make_pair(L.theta, L.rope_scale);
+      const float2 *found = nullptr;
+      for (auto &kv : ctx->rope_tables)
+        if (kv.first == key) found = kv.second;
+      if (!found) {
+        float2 *dev = nullptr;
+        if ((rc = ctx_alloc_t(ctx, &dev, host.size(), "rope table"))) return rc;
+        for (int pos = 0; pos < ctx->context; pos++)
+          for (int i = 0; i < half; i++) {
+            const double angle = (double)pos * L.rope_scale / std::pow(L.theta, (2.0 * i) / rot);
+            host[(size_t)pos * half + i] = make_float2((float)std::cos(angle), (float)std::sin(angle));
+          }
+        CK(cudaMemcpy(dev, host.data(), host.size() * sizeof(float2), cudaMemcpyHostToDevice));
+        ctx->rope_tables.push_back({key, dev});
+        found = dev;
+      }
+      L.rope_table = found;
+    }
+  }
   if (ctx->g2_part_floats && ((rc = ctx_alloc_t(ctx, &ctx->g2_part, ctx->g2_part_floats, "gemv partials")) ||
                               (rc = ctx_alloc_t(ctx, &ctx->g2_ctr, (size_t)ctx->g2_ctr_count, "gemv tile counters"))))
     return rc;
@@ -712,7 +739,7 @@ static int enqueue_forward(wgd_ctx *ctx, int n, bool want_logits_rows, bool io =
     CK(cudaMemcpyAsync(ctx->d_start, ctx->h_io, sizeof(int32_t), cudaMemcpyHostToDevice, ctx->stream));
     CK(cudaMemcpyAsync(ctx->d_ids, ctx->h_io + 2, sizeof(int32_t) * n, cudaMemcpyHostToDevice, ctx->stream));
   }
-  ctx->kernels += 1 + c.layers * 2 + 1 + (gemma ? 2 * c.layers : 0) + (tp1 ? 0 : (gemma ? 2 : 2) * c.layers + 1);
+  ctx->kernels += 1 + c.layers * 1 + 1 + (gemma ? 2 * c.layers : 0) + (tp1 ? 0 : 2 * c.layers + 1);
   CK(launch_embed(ctx->embd.type, ctx->embd.w, ctx->embd.drow, H, ctx->d_ids, n, c.vocab, gemma ? sqrtf((float)H) : 1.f,
                   ctx->hidden, H, ctx->d_err, ctx->stream, false, ctx->embd.tiled));
   for (int l = 0; l < c.layers; l++) {
@@ -733,12 +760,17 @@ static int enqueue_forward(wgd_ctx *ctx, int n, bool want_logits_rows, bool io =
     ra.eps = c.epsilon;
     ra.theta = L.theta;
     ra.scale = L.rope_scale;
+    ra.table = L.rope_table;
     ra.start = ctx->d_start;
     ra.k_cache = L.k_cache;
     ra.v_cache = L.v_cache;
     ra.capacity = L.capacity;
     ra.q_out = ctx->qrot;
-    CK(launch_rope_kv(ra, ctx->stream, true));
+    const bool fuse_rope = n == 1;  // decode: the attention kernel rotates and writes the new K/V itself
+    if (!fuse_rope) {
+      CK(launch_rope_kv(ra, ctx->stream, true));
+      ctx->kernels += 1;
+    }
     AttnArgs aa{};
     aa.q = ctx->qrot;
     aa.k = L.k_cache;
@@ -755,6 +787,15 @@ static int enqueue_forward(wgd_ctx *ctx, int n, bool want_logits_rows, bool io =
     aa.part = ctx->att_part;
     aa.ctr = ctx->att_ctr;
     aa.splits = ctx->att_splits;
+    if (fuse_rope) {
+      aa.qkv = ctx->qkv;
+      aa.q_norm = L.q_norm;
+      aa.k_norm = L.k_norm;
+      aa.eps = c.epsilon;
+      aa.rot = ra.rot;
+      aa.mode = ra.mode;
+      aa.table = L.rope_table;
+    }
     CK(launch_attention(aa, ctx->stream, true));
     if (gemma) {
       if ((rc = gemv(ctx, L.o, ctx->att, ctx->q_l, nullptr, ctx->proj, H, nullptr, EPI_STORE, n))) return rc;

@@ -104,6 +104,7 @@ struct RopeArgs {
   const float *q_norm, *k_norm;  // per-head RMS weights (qk-norm) or null
   float eps;
   double theta, scale;
+  const float2 *table; // (cos, sin) of pos*scale/theta^(2i/rot), [context][rot/2]; null: computed in double
   const int *start;    // device int: absolute position of row 0
   int start_host;      // used when start == nullptr
   float *k_cache, *v_cache;  // [kv_heads][capacity][hd]
@@ -120,9 +121,17 @@ struct AttnArgs {
   float scale;
   const int *start;    // device int or null (then start_host)
   int start_host;
-  float *part;         // scratch: [n][kv_heads][splits][group*(hd+2)]
+  float *part;         // scratch: [n][kv_heads][splits][group][hd + 4] (16-byte aligned)
   unsigned *ctr;       // [n * kv_heads] zeroed counters (left zeroed)
   int splits;          // grid.y
+  // decode (n == 1) with the RoPE/KV write fused in: q/k/v are read raw from `qkv`,
+  // rotated (after the optional per-head norm) with `table`, and the new K/V row is
+  // written to ring slot start % capacity of k/v by the CTA that owns that position.
+  const float *qkv;    // non-null: fused mode; row 0 = q heads | k heads | v heads
+  const float *q_norm, *k_norm;
+  float eps;
+  int rot, mode;
+  const float2 *table;
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl);
 int attention_splits(int max_len);

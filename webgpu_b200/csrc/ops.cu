@@ -231,10 +231,18 @@ __global__ void rope_kv_kernel(const RopeArgs a) {
   }
   const int rot = a.rot, half = rot / 2;
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
-    const double angle = (double)pos * a.scale / pow(a.theta, (2.0 * i) / rot);
-    double sn, cs;
-    sincos(angle, &sn, &cs);
-    const float c = (float)cs, s = (float)sn;
+    float c, s;
+    if (a.table) {
+      const float2 cs2 = a.table[(int64_t)pos * half + i];
+      c = cs2.x;
+      s = cs2.y;
+    } else {
+      const double angle = (double)pos * a.scale / pow(a.theta, (2.0 * i) / rot);
+      double sn, cs;
+      sincos(angle, &sn, &cs);
+      c = (float)cs;
+      s = (float)sn;
+    }
     const int ia = a.mode == 0 ? i : 2 * i, ib = a.mode == 0 ? i + half : 2 * i + 1;
     const float l = hv[ia], r = hv[ib];
     hv[ia] = l * c - r * s;
@@ -262,188 +270,303 @@ cudaError_t launch_rope_kv(const RopeArgs &a, cudaStream_t s, bool pdl) {
 
 // ------------------------------------------------------------------ attention
 
-// Split-K decode attention with an in-kernel merge (flash-decoding). CTA
+// Split-K attention with an in-kernel merge (flash-decoding). CTA
 // (t*kv_heads + kh, sp) scores keys [p0, p1) of query row t against all G =
-// heads/kv_heads query heads of KV head kh, keeps an online softmax (max, sum,
-// weighted V) over 128-key tiles, and writes a partial; the last CTA of the
-// (t, kh) pair merges the partials in split order. Keys are read from ring slot
-// p % capacity of the [kv_heads][capacity][hd] cache (attentionShader
-// semantics: window [end - min(end, window), end), end = start + t + 1).
-constexpr int ATT_THREADS = 128, ATT_TILE = 128, ATT_GMAX = 8, ATT_MINCHUNK = 64, ATT_MAXSPLIT = 64;
+// heads/kv_heads query heads of KV head kh and writes a partial (running max,
+// sum, weighted V); the last CTA of the (t, kh) pair merges the partials in
+// split order. Keys are read from ring slot p % capacity of the
+// [kv_heads][capacity][hd] cache (attentionShader semantics: window
+// [end - min(end, window), end), end = start + t + 1).
+//
+// K and V rows are staged 32 at a time into shared memory with cp.async (two
+// stages when they fit), rows padded to hd + 4 floats so that lane-per-row
+// reads are bank-conflict free. Warp w owns query heads w and w + 4: lane j
+// scores key j of the tile, the online softmax lives in registers, and for PV
+// lane l accumulates dims [4l, 4l + 4) (+128 per extra float4) of its heads.
+constexpr int ATT_THREADS = 128, ATT_WARPS = 4, ATT_TILE = 32, ATT_GMAX = 8, ATT_MAXSPLIT = 64;
+constexpr int ATT_CHUNK_DECODE = 32, ATT_CHUNK_ROWS = 64;
 
 int attention_splits(int max_len) {
-  int s = (max_len + ATT_MINCHUNK - 1) / ATT_MINCHUNK;
+  int s = (max_len + ATT_CHUNK_DECODE - 1) / ATT_CHUNK_DECODE;
   return s < 1 ? 1 : s > ATT_MAXSPLIT ? ATT_MAXSPLIT : s;
 }
 size_t attention_part_floats(int n, int heads, int kv_heads, int hd, int splits) {
-  return (size_t)n * kv_heads * splits * (heads / kv_heads) * (hd + 2);
+  return (size_t)n * kv_heads * splits * (heads / kv_heads) * (hd + 4);
 }
 
+__device__ __forceinline__ void cp_async16(void *smem, const void *g) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ float4 f4_fma(float s, float4 v, float4 a) {
+  return make_float4(fmaf(s, v.x, a.x), fmaf(s, v.y, a.y), fmaf(s, v.z, a.z), fmaf(s, v.w, a.w));
+}
+
+// NI = float4s per lane per head row (hd <= 128 * NI).
+template <int NI>
 __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnArgs a) {
-  extern __shared__ float sm[];
-  const int G = a.heads / a.kv_heads, hd = a.hd;
-  float *q_s = sm;                          // [G][hd]
-  float *e_s = q_s + G * hd;                // [G][ATT_TILE]
-  float *red = e_s + G * ATT_TILE;          // [G][4] warp partials
-  float *acc_s = red + G * 4;               // [G][hd] position-group partials
-  __shared__ float m_s[ATT_GMAX], l_s[ATT_GMAX], corr_s[ATT_GMAX];
+  extern __shared__ __align__(16) float sm[];
+  const int G = a.heads / a.kv_heads, hd = a.hd, hd4 = hd >> 2, RS = hd + 4;
+  const int nst = hd <= 256 ? 2 : 1;
+  float *q_s = sm;              // [G][hd]
+  float *kn_s = q_s + G * hd;   // new K row (fused decode)
+  float *vn_s = kn_s + hd;      // new V row
+  float *kv_s = vn_s + hd;      // [nst][K|V][ATT_TILE][RS]
   __shared__ int last_s;
-  pdl_wait();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int t = blockIdx.x / a.kv_heads, kh = blockIdx.x % a.kv_heads, sp = blockIdx.y;
+  const bool fused = a.qkv != nullptr;
+  // In fused decode mode every cached row but the new one was written by an
+  // earlier token's kernels (already complete), and `start` by the previous
+  // step's advance kernel, so staging may begin before the dependency wait.
+  if (!fused) pdl_wait();
   const int start = a.start ? *a.start : a.start_host;
   const int end = start + t + 1, begin = end - (end < a.window ? end : a.window), L = end - begin;
+  const int minc = a.n == 1 ? ATT_CHUNK_DECODE : ATT_CHUNK_ROWS;
   int chunk = (L + a.splits - 1) / a.splits;
-  if (chunk < ATT_MINCHUNK) chunk = ATT_MINCHUNK;
+  if (chunk < minc) chunk = minc;
   const int nsp = (L + chunk - 1) / chunk;
-  if (sp >= nsp) return;
+  if (sp >= nsp) {
+    if (fused) pdl_wait();
+    return;
+  }
   const int p0 = begin + sp * chunk, p1 = min(end, p0 + chunk);
-
-  for (int i = tid; i < G * hd; i += ATT_THREADS) q_s[i] = a.q[((int64_t)t * a.heads + kh * G) * hd + i];
-  if (tid < G) { m_s[tid] = -FLT_MAX; l_s[tid] = 0.f; }
-  // PV mapping: thread handles dims d = dsub + 128k of position group pg.
-  const int dlanes = hd < ATT_THREADS ? hd : ATT_THREADS;
-  const int pgroups = ATT_THREADS / dlanes;
-  const int dsub = tid % dlanes, pg = tid / dlanes;
-  const bool pv_live = pg < pgroups;
-  float acc[ATT_GMAX][4];
-#pragma unroll
-  for (int g = 0; g < ATT_GMAX; g++)
-#pragma unroll
-    for (int k = 0; k < 4; k++) acc[g][k] = 0.f;
+  const bool owns_new = fused && p1 == end;  // this CTA scores the new position
   const float *kb = a.k + (int64_t)kh * a.capacity * hd;
   const float *vb = a.v + (int64_t)kh * a.capacity * hd;
-  __syncthreads();
+  const int ntiles = (p1 - p0 + ATT_TILE - 1) / ATT_TILE;
 
-  for (int tile = p0; tile < p1; tile += ATT_TILE) {
-    const int p = tile + tid;
-    const bool live = p < p1;
-    float s[ATT_GMAX];
+  auto stage = [&](int tile, int st) {
+    const int cnt = min(ATT_TILE, p1 - tile), total = cnt * hd4;
+    float *ks = kv_s + (size_t)st * 2 * ATT_TILE * RS, *vs = ks + ATT_TILE * RS;
+    for (int i = tid; i < total; i += ATT_THREADS) {
+      const int r = i / hd4, c = (i - r * hd4) * 4;
+      const int p = tile + r;
+      if (owns_new && p == end - 1) continue;  // filled from shared memory below
+      const int64_t row = (int64_t)(p % a.capacity) * hd;
+      cp_async16(ks + r * RS + c, kb + row + c);
+      cp_async16(vs + r * RS + c, vb + row + c);
+    }
+    cp_async_commit();
+  };
+  stage(p0, 0);
+  if (nst == 2 && ntiles > 1) stage(p0 + ATT_TILE, 1);
+
+  if (fused) pdl_wait();
+  if (!fused) {
+    for (int i = tid; i < G * hd; i += ATT_THREADS) q_s[i] = a.q[((int64_t)t * a.heads + kh * G) * hd + i];
+  } else {
+    const int hq = G + (owns_new ? 1 : 0);  // q heads, then the k head when this CTA owns the new row
+    for (int i = tid; i < hq * hd; i += ATT_THREADS) {
+      const int g = i / hd, d = i - g * hd;
+      const float *src = g < G ? a.qkv + (int64_t)(kh * G + g) * hd : a.qkv + (int64_t)(a.heads + kh) * hd;
+      (g < G ? q_s + g * hd : kn_s)[d] = src[d];
+    }
+    if (owns_new)
+      for (int d = tid; d < hd; d += ATT_THREADS) vn_s[d] = a.qkv[(int64_t)(a.heads + a.kv_heads + kh) * hd + d];
+    __syncthreads();
+    // per-head RMS norm (Q/K norm) then rotation, one warp per head
+    for (int g = warp; g < hq; g += ATT_WARPS) {
+      float *hv = g < G ? q_s + g * hd : kn_s;
+      const float *nw = g < G ? a.q_norm : a.k_norm;
+      if (nw) {
+        float ss = 0.f;
+        for (int d = lane; d < hd; d += 32) ss = fmaf(hv[d], hv[d], ss);
+        const float inv = rsqrtf(warp_sum(ss) / (float)hd + a.eps);
+        __syncwarp();
+        for (int d = lane; d < hd; d += 32) hv[d] = hv[d] * inv * nw[d];
+        __syncwarp();
+      }
+      const int half = a.rot / 2;
+      const float2 *tb = a.table + (int64_t)start * half;
+      for (int i = lane; i < half; i += 32) {
+        const float2 cs = tb[i];
+        const int ia = a.mode == 0 ? i : 2 * i, ib = a.mode == 0 ? i + half : 2 * i + 1;
+        const float l = hv[ia], r = hv[ib];
+        hv[ia] = l * cs.x - r * cs.y;
+        hv[ib] = l * cs.y + r * cs.x;
+      }
+      __syncwarp();
+    }
+    __syncthreads();
+    if (owns_new) {  // the ring slot of the new position, for later steps
+      const int slot = start % a.capacity;
+      float *kd = const_cast<float *>(a.k) + ((int64_t)kh * a.capacity + slot) * hd;
+      float *vd = const_cast<float *>(a.v) + ((int64_t)kh * a.capacity + slot) * hd;
+      for (int d = tid; d < hd; d += ATT_THREADS) { kd[d] = kn_s[d]; vd[d] = vn_s[d]; }
+    }
+  }
+
+  const int g0 = warp, g1 = warp + ATT_WARPS;
+  const bool h0 = g0 < G, h1 = g1 < G;
+  float m0 = -FLT_MAX, m1 = -FLT_MAX, l0 = 0.f, l1 = 0.f;
+  float4 acc0[NI], acc1[NI];
 #pragma unroll
-    for (int g = 0; g < ATT_GMAX; g++) s[g] = 0.f;
-    if (live) {
-      const float4 *kr = reinterpret_cast<const float4 *>(kb + (int64_t)(p % a.capacity) * hd);
-      for (int d4 = 0; d4 < hd / 4; d4++) {
-        const float4 k4 = __ldg(kr + d4);
+  for (int i = 0; i < NI; i++) acc0[i] = acc1[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  for (int ti = 0; ti < ntiles; ti++) {
+    const int tile = p0 + ti * ATT_TILE, cnt = min(ATT_TILE, p1 - tile);
+    const int st = nst == 2 ? (ti & 1) : 0;
+    if (nst == 2 && ti + 1 < ntiles) cp_async_wait<1>(); else cp_async_wait<0>();
+    __syncthreads();
+    float *ks = kv_s + (size_t)st * 2 * ATT_TILE * RS, *vs = ks + ATT_TILE * RS;
+    if (owns_new && tile + cnt == end) {  // block-uniform
+      const int r = end - 1 - tile;
+      for (int d = tid; d < hd; d += ATT_THREADS) { ks[r * RS + d] = kn_s[d]; vs[r * RS + d] = vn_s[d]; }
+      __syncthreads();
+    }
+    // scores: lane j <-> key tile + j
+    const bool live = lane < cnt;
+    float s0 = 0.f, s1 = 0.f;
+    {
+      const float4 *kr = reinterpret_cast<const float4 *>(ks + lane * RS);
+      const float4 *q0 = reinterpret_cast<const float4 *>(q_s + g0 * hd);
+      const float4 *q1 = reinterpret_cast<const float4 *>(q_s + (h1 ? g1 : g0) * hd);
+#pragma unroll 8
+      for (int d4 = 0; d4 < hd4; d4++) {
+        const float4 k4 = kr[d4];
+        if (h0) {
+          const float4 q = q0[d4];
+          s0 = fmaf(q.x, k4.x, fmaf(q.y, k4.y, fmaf(q.z, k4.z, fmaf(q.w, k4.w, s0))));
+        }
+        if (h1) {
+          const float4 q = q1[d4];
+          s1 = fmaf(q.x, k4.x, fmaf(q.y, k4.y, fmaf(q.z, k4.z, fmaf(q.w, k4.w, s1))));
+        }
+      }
+    }
+    float e0 = 0.f, e1 = 0.f;
+    if (h0) {
+      s0 = live ? s0 * a.scale : -FLT_MAX;
+      const float mn = fmaxf(m0, warp_max(s0)), corr = expf(m0 - mn);
+      e0 = live ? expf(s0 - mn) : 0.f;
+      l0 = fmaf(l0, corr, warp_sum(e0));
+      m0 = mn;
 #pragma unroll
-        for (int g = 0; g < ATT_GMAX; g++) {
-          if (g < G) {
-            const float4 q4 = reinterpret_cast<const float4 *>(q_s + g * hd)[d4];
-            s[g] = fmaf(q4.x, k4.x, fmaf(q4.y, k4.y, fmaf(q4.z, k4.z, fmaf(q4.w, k4.w, s[g]))));
+      for (int i = 0; i < NI; i++) acc0[i] = make_float4(acc0[i].x * corr, acc0[i].y * corr, acc0[i].z * corr, acc0[i].w * corr);
+    }
+    if (h1) {
+      s1 = live ? s1 * a.scale : -FLT_MAX;
+      const float mn = fmaxf(m1, warp_max(s1)), corr = expf(m1 - mn);
+      e1 = live ? expf(s1 - mn) : 0.f;
+      l1 = fmaf(l1, corr, warp_sum(e1));
+      m1 = mn;
+#pragma unroll
+      for (int i = 0; i < NI; i++) acc1[i] = make_float4(acc1[i].x * corr, acc1[i].y * corr, acc1[i].z * corr, acc1[i].w * corr);
+    }
+    if (h0) {
+#pragma unroll 4
+      for (int j = 0; j < cnt; j++) {
+        const float w0 = __shfl_sync(0xffffffffu, e0, j), w1 = __shfl_sync(0xffffffffu, e1, j);
+        const float4 *vr = reinterpret_cast<const float4 *>(vs + j * RS);
+#pragma unroll
+        for (int i = 0; i < NI; i++) {
+          const int d4 = lane + 32 * i;
+          if (d4 < hd4) {
+            const float4 v = vr[d4];
+            acc0[i] = f4_fma(w0, v, acc0[i]);
+            if (h1) acc1[i] = f4_fma(w1, v, acc1[i]);
           }
         }
       }
     }
-    // tile max per head
-#pragma unroll
-    for (int g = 0; g < ATT_GMAX; g++) {
-      if (g < G) {
-        s[g] = live ? s[g] * a.scale : -FLT_MAX;
-        float mx = warp_max(s[g]);
-        if (lane == 0) red[g * 4 + warp] = mx;
-      }
-    }
-    __syncthreads();
-    if (tid < G) {
-      float mx = fmaxf(fmaxf(red[tid * 4], red[tid * 4 + 1]), fmaxf(red[tid * 4 + 2], red[tid * 4 + 3]));
-      float mnew = fmaxf(m_s[tid], mx);
-      corr_s[tid] = expf(m_s[tid] - mnew);
-      m_s[tid] = mnew;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int g = 0; g < ATT_GMAX; g++) {
-      if (g < G) {
-        float e = live ? expf(s[g] - m_s[g]) : 0.f;
-        e_s[g * ATT_TILE + tid] = e;
-        float sum = warp_sum(e);
-        if (lane == 0) red[g * 4 + warp] = sum;
-      }
-    }
-    __syncthreads();
-    if (tid < G) l_s[tid] = l_s[tid] * corr_s[tid] + ((red[tid * 4] + red[tid * 4 + 1]) + (red[tid * 4 + 2] + red[tid * 4 + 3]));
-    // PV over this tile
-    const int cnt = min(ATT_TILE, p1 - tile);
-#pragma unroll
-    for (int g = 0; g < ATT_GMAX; g++)
-      if (g < G)
-#pragma unroll
-        for (int k = 0; k < 4; k++) acc[g][k] *= corr_s[g];
-    for (int j = pg; pv_live && j < cnt; j += pgroups) {
-      const float *vr = vb + (int64_t)((tile + j) % a.capacity) * hd;
-#pragma unroll
-      for (int k = 0; k < 4; k++) {
-        const int d = dsub + k * ATT_THREADS;
-        if (d < hd) {
-          const float v = __ldg(vr + d);
-#pragma unroll
-          for (int g = 0; g < ATT_GMAX; g++)
-            if (g < G) acc[g][k] = fmaf(e_s[g * ATT_TILE + j], v, acc[g][k]);
-        }
-      }
-    }
-    __syncthreads();
+    __syncthreads();  // stage st is free again
+    if (nst == 2 && ti + 2 < ntiles) stage(tile + 2 * ATT_TILE, st);
+    else if (nst == 1 && ti + 1 < ntiles) stage(tile + ATT_TILE, 0);
   }
-  // combine position groups into acc_s[g][d]
-  for (int i = tid; i < G * hd; i += ATT_THREADS) acc_s[i] = 0.f;
-  __syncthreads();
-  for (int q = 0; q < pgroups; q++) {
-    if (pg == q) {
-#pragma unroll
-      for (int g = 0; g < ATT_GMAX; g++)
-        if (g < G)
-#pragma unroll
-          for (int k = 0; k < 4; k++) {
-            const int d = dsub + k * ATT_THREADS;
-            if (d < hd) acc_s[g * hd + d] += acc[g][k];
-          }
-    }
-    __syncthreads();
-  }
+
   const int pair = t * a.kv_heads + kh;
   float *out_base = a.out + ((int64_t)t * a.heads + kh * G) * hd;
   if (nsp == 1) {
-    for (int i = tid; i < G * hd; i += ATT_THREADS) out_base[i] = acc_s[i] / l_s[i / hd];
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+      const int d4 = lane + 32 * i;
+      if (d4 < hd4) {
+        if (h0) reinterpret_cast<float4 *>(out_base + g0 * hd)[d4] =
+            make_float4(acc0[i].x / l0, acc0[i].y / l0, acc0[i].z / l0, acc0[i].w / l0);
+        if (h1) reinterpret_cast<float4 *>(out_base + g1 * hd)[d4] =
+            make_float4(acc1[i].x / l1, acc1[i].y / l1, acc1[i].z / l1, acc1[i].w / l1);
+      }
+    }
     pdl_launch_dependents();
     return;
   }
-  float *part = a.part + ((int64_t)pair * a.splits + sp) * G * (hd + 2);
-  for (int i = tid; i < G * hd; i += ATT_THREADS) part[(i / hd) * (hd + 2) + 2 + (i % hd)] = acc_s[i];
-  if (tid < G) { part[tid * (hd + 2)] = m_s[tid]; part[tid * (hd + 2) + 1] = l_s[tid]; }
+  // partial row per (pair, split, head): acc[hd] | m | l | pad (stride hd + 4)
+  const int PR = hd + 4;
+  float *part = a.part + ((int64_t)pair * a.splits + sp) * G * PR;
+#pragma unroll
+  for (int i = 0; i < NI; i++) {
+    const int d4 = lane + 32 * i;
+    if (d4 < hd4) {
+      if (h0) reinterpret_cast<float4 *>(part + g0 * PR)[d4] = acc0[i];
+      if (h1) reinterpret_cast<float4 *>(part + g1 * PR)[d4] = acc1[i];
+    }
+  }
+  if (lane == 0) {
+    if (h0) { part[g0 * PR + hd] = m0; part[g0 * PR + hd + 1] = l0; }
+    if (h1) { part[g1 * PR + hd] = m1; part[g1 * PR + hd + 1] = l1; }
+  }
   __threadfence();
   __syncthreads();
   if (tid == 0) last_s = atomicAdd(a.ctr + pair, 1u) == (unsigned)(nsp - 1);
   __syncthreads();
   if (!last_s) return;
   __threadfence();
-  const float *pb = a.part + (int64_t)pair * a.splits * G * (hd + 2);
-  for (int i = tid; i < G * hd; i += ATT_THREADS) {
-    const int g = i / hd, d = i % hd;
-    float M = -FLT_MAX;
-    for (int j = 0; j < nsp; j++) M = fmaxf(M, __ldcg(pb + ((int64_t)j * G + g) * (hd + 2)));
-    float num = 0.f, den = 0.f;
-    for (int j = 0; j < nsp; j++) {
-      const float *pp = pb + ((int64_t)j * G + g) * (hd + 2);
-      const float w = expf(__ldcg(pp) - M);
-      den = fmaf(w, __ldcg(pp + 1), den);
-      num = fmaf(w, __ldcg(pp + 2 + d), num);
+  const float *pb = a.part + (int64_t)pair * a.splits * G * PR;
+  const int64_t sstride = (int64_t)G * PR;  // one split
+  for (int g = warp; g < G; g += ATT_WARPS) {
+    const float *ph = pb + g * PR;
+    // split j's weight exp(m_j - M) / sum, held by lane j % 32 (j < 64)
+    const float ma = lane < nsp ? __ldcg(ph + lane * sstride + hd) : -FLT_MAX;
+    const float mb = lane + 32 < nsp ? __ldcg(ph + (lane + 32) * sstride + hd) : -FLT_MAX;
+    const float M = warp_max(fmaxf(ma, mb));
+    const float wa = lane < nsp ? expf(ma - M) : 0.f, wb = lane + 32 < nsp ? expf(mb - M) : 0.f;
+    const float la = lane < nsp ? __ldcg(ph + lane * sstride + hd + 1) : 0.f;
+    const float lb = lane + 32 < nsp ? __ldcg(ph + (lane + 32) * sstride + hd + 1) : 0.f;
+    const float den = warp_sum(fmaf(wa, la, wb * lb));
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+      const int d4 = lane + 32 * i;
+      float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+      for (int j = 0; j < nsp; j++) {
+        const float w = __shfl_sync(0xffffffffu, j < 32 ? wa : wb, j & 31);
+        if (d4 < hd4) num = f4_fma(w, __ldcg(reinterpret_cast<const float4 *>(ph + j * sstride) + d4), num);
+      }
+      if (d4 < hd4) reinterpret_cast<float4 *>(out_base + g * hd)[d4] = make_float4(num.x / den, num.y / den, num.z / den, num.w / den);
     }
-    out_base[i] = num / den;
   }
   if (tid == 0) a.ctr[pair] = 0u;
   pdl_launch_dependents();
 }
 
+template <int NI>
+static cudaError_t launch_attention_ni(const AttnArgs &a, size_t smem, cudaStream_t s, bool pdl) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel<NI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  return launch_k(attention_kernel<NI>, dim3(a.n * a.kv_heads, a.splits), dim3(ATT_THREADS), smem, s, pdl, a);
+}
+
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
   const int G = a.heads / a.kv_heads;
   if (G > ATT_GMAX || a.hd % 4 || a.hd > 4 * ATT_THREADS || a.splits < 1 || a.splits > ATT_MAXSPLIT) return cudaErrorInvalidValue;
-  size_t smem = sizeof(float) * ((size_t)G * a.hd * 2 + (size_t)G * ATT_TILE + G * 4);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
-  }
-  return launch_k(attention_kernel, dim3(a.n * a.kv_heads, a.splits), dim3(ATT_THREADS), smem, s, pdl, a);
+  if ((reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.out) |
+       reinterpret_cast<uintptr_t>(a.part)) & 15)
+    return cudaErrorMisalignedAddress;
+  const int nst = a.hd <= 256 ? 2 : 1;
+  const size_t smem = sizeof(float) * ((size_t)G * a.hd + 2 * (size_t)a.hd + (size_t)nst * 2 * ATT_TILE * (a.hd + 4));
+  if (a.hd <= 128) return launch_attention_ni<1>(a, smem, s, pdl);
+  if (a.hd <= 256) return launch_attention_ni<2>(a, smem, s, pdl);
+  return launch_attention_ni<4>(a, smem, s, pdl);
 }
 
 // ------------------------------------------------------------------ argmax
