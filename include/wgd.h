@@ -170,6 +170,13 @@ WGD_API int wgd_op_dequant_tiled(int ggml_type, int64_t rows, int64_t cols, cons
 /* The same product as wgd_op_gemv over tiled weights (integer tensor-core path). */
 WGD_API int wgd_op_gemv_tiled(int ggml_type, int64_t rows, int64_t cols, const void *tiled_dev, const float *x_dev, int batch,
                               float *y_dev, void *stream);
+/* wgd_op_gemv_tiled for callers that may not allocate device memory while running (no counterpart in
+ * the reference, whose WebGPU path has no such constraint): the scratch is a fixed per-device array of
+ * 4 MiB of partial sums and 8192 tile counters, and shapes needing more fail with WGD_EINVAL. The first
+ * call on a device (that device current) sets the scratch up and should come before any stream capture;
+ * later calls allocate nothing. Calls on one device must not overlap in time: they share the scratch. */
+WGD_API int wgd_op_gemv_tiled_noalloc(int ggml_type, int64_t rows, int64_t cols, const void *tiled_dev, const float *x_dev,
+                                      int batch, float *y_dev, void *stream);
 /* RMSNorm of n rows (normShader, shaders.ts:84-97). */
 WGD_API int wgd_op_rmsnorm(const float *x_dev, const float *w_dev, int cols, int n, float eps, float *y_dev, void *stream);
 /* Q/K rotation (+ optional per-head RMS norm) of x[n][heads][hd] in place:

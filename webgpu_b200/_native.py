@@ -74,6 +74,7 @@ SIGNATURES = {
     "wgd_op_repack_tiled": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "wgd_op_dequant_tiled": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "wgd_op_gemv_tiled": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "wgd_op_gemv_tiled_noalloc": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "wgd_op_rmsnorm": (c_int, [c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_void_p]),
     "wgd_op_rope": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_float, c_float, c_int, c_int, c_void_p]),
     "wgd_op_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_int,

@@ -35,6 +35,10 @@ static int fail(int code, const std::string &msg) {
   g_err = msg;
   return code;
 }
+namespace wgd {
+// Sets the thread's wgd_last_error() text for entry points defined in other files.
+int api_fail(int code, const std::string &msg) { return fail(code, msg); }
+}  // namespace wgd
 #define CK(call)                                                                                  \
   do {                                                                                            \
     cudaError_t e_ = (call);                                                                      \
