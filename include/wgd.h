@@ -75,6 +75,7 @@ typedef struct wgd_stats {
   uint64_t forwards, tokens;
   double last_forward_ms;   /* device time of the last forward (CUDA events) */
   uint64_t streamed_bytes;  /* weight bytes streamed through page slots by the last forward */
+  uint64_t kernel_launches; /* kernels this library launched for forwards and decodes, cumulative */
 } wgd_stats;
 
 typedef struct wgd_ctx wgd_ctx;
@@ -136,7 +137,7 @@ WGD_API int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, int 
  * engine.ts:290-297, with sample() on the device). tokens_out receives the
  * `steps` generated ids (stopping early is the caller's business). */
 WGD_API int wgd_decode(wgd_ctx *ctx, int32_t first, int start, int steps, int32_t *tokens_out);
-/* Number of kernels one single-token forward launches (for launch accounting). */
+/* Kernels launched by the last forward (per token) or persistent call (1), for launch accounting. */
 WGD_API int wgd_kernels_per_token(wgd_ctx *ctx, int *count);
 /* KV cache bookkeeping for prefix reuse and reset (engine.ts:269-283,302). */
 WGD_API int wgd_truncate_kv(wgd_ctx *ctx, int n_tokens);
@@ -144,6 +145,13 @@ WGD_API void wgd_cancel(wgd_ctx *ctx);
 WGD_API int wgd_stats_get(wgd_ctx *ctx, wgd_stats *out);
 /* Enables/disables CUDA-graph replay of single-token forwards (default on). */
 WGD_API int wgd_set_graphs(wgd_ctx *ctx, int enabled);
+/* Enables/disables the persistent decode kernel (default on): single-row forwards and wgd_decode
+ * then run as one cooperative launch per call (all layers, LM head, argmax, token feedback) when the
+ * model's shapes allow it; otherwise, or when disabled, they use the per-kernel path. */
+WGD_API int wgd_set_persistent(wgd_ctx *ctx, int enabled);
+/* 1 when the persistent decode kernel is available for this model, 0 when not (the reason is
+ * written to why[0..why_len)). */
+WGD_API int wgd_persistent_status(wgd_ctx *ctx, char *why, int why_len);
 
 /* ---------------------------------------------------------------- kernels
  * Single-kernel entry points on caller-owned device memory, on `stream`

@@ -35,7 +35,7 @@ class StatsC(ctypes.Structure):
     _fields_ = [("read_bytes", c_uint64), ("uploads", c_uint64), ("cache_hits", c_uint64), ("cache_bytes", c_uint64),
                 ("gpu_bytes", c_uint64), ("peak_gpu_bytes", c_uint64), ("page_bytes", c_uint64), ("read_ms", ctypes.c_double),
                 ("forwards", c_uint64), ("tokens", c_uint64), ("last_forward_ms", ctypes.c_double),
-                ("streamed_bytes", c_uint64)]
+                ("streamed_bytes", c_uint64), ("kernel_launches", c_uint64)]
 
 
 READ_FN = ctypes.CFUNCTYPE(c_int, c_void_p, c_uint64, c_uint64, c_void_p)
@@ -66,6 +66,8 @@ SIGNATURES = {
     "wgd_cancel": (None, [c_void_p]),
     "wgd_stats_get": (c_int, [c_void_p, ctypes.POINTER(StatsC)]),
     "wgd_set_graphs": (c_int, [c_void_p, c_int]),
+    "wgd_set_persistent": (c_int, [c_void_p, c_int]),
+    "wgd_persistent_status": (c_int, [c_void_p, c_char_p, c_int]),
     "wgd_dev_row_bytes": (c_int64, [c_int, c_int64]),
     "wgd_op_repack": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "wgd_op_dequant": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),

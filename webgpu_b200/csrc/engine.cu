@@ -25,6 +25,7 @@
 #include "../../include/wgd.h"
 #include "common.cuh"
 #include "kernels.h"
+#include "persist.h"
 #include "tile.cuh"
 #include "tp.h"
 
@@ -139,12 +140,20 @@ struct wgd_ctx {
   cudaGraph_t decode_graph = nullptr, chain_graph = nullptr;
   int *d_tokens = nullptr, *d_step = nullptr;
   int kernels = 0;  // kernels launched by the last enqueued forward
+  int decode_kernels = 0, chain_kernels = 0;  // kernels in the captured graphs
   std::atomic<int> cancel{0};
   wgd_stats st{};
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   TpComm *tp = nullptr;
   uint64_t tp_spin_limit = 0;
+  // persistent decode kernel (one launch per wgd_forward of one row / per wgd_decode)
+  bool persist_ok = false, persist_on = true;
+  std::string persist_why = "not built";
+  PersistArgs pargs{};
+  int *h_status = nullptr;  // pinned mirror of pargs.status
 };
+// h_io slots: [0] start, [1] argmax, [2..1015] ids, [1016..1019] persistent status, [1020] cancel word
+constexpr int IO_STATUS = 1016, IO_CANCEL = 1020;
 
 // ------------------------------------------------------------------ helpers
 
@@ -376,6 +385,165 @@ static int place_vec(wgd_ctx *ctx, TensorRec *t, float *dst, int src0, int len) 
   return WGD_OK;
 }
 
+// The persistent decode plan: one PPhase per projection / attention of every layer,
+// then the LM head. Built only for shapes the kernel covers; otherwise decode
+// keeps the per-kernel path (persist_why says why).
+static int build_persist_plan(wgd_ctx *ctx) {
+  const wgd_model_config &c = ctx->c;
+  const int H = c.hidden, hd = c.head_dim;
+  ctx->persist_ok = false;
+  auto no = [&](const char *why) { ctx->persist_why = why; return WGD_OK; };
+  if (ctx->tp_size != 1) return no("tensor-parallel runs use the per-kernel path");
+  if (c.family == 1) return no("the gemma block (post-norms) uses the per-kernel path");
+  const int G = ctx->kv_l ? ctx->heads_l / ctx->kv_l : 0;
+  if (hd % 4 || hd > 256 || G < 1 || G > 8) return no("attention shape outside the persistent kernel");
+  auto tiled_ok = [](const DevLinear &L) { return L.tiled && L.cols % 256 == 0 && L.cols / 256 >= 8; };
+  if (!tiled_ok(ctx->lm)) return no("the LM head is not in the tiled layout");
+  int max_cols = H;
+  for (auto &L : ctx->layers) {
+    if (!tiled_ok(L.qkv) || !tiled_ok(L.o) || !tiled_ok(L.gate_up) || !tiled_ok(L.down))
+      return no("a projection is not in the tiled layout (Q4_K/Q6_K, width >= 2048)");
+    max_cols = std::max(max_cols, std::max(L.o.cols, L.down.cols));
+  }
+  if (max_cols > 16384) return no("a projection input is wider than the kernel's digit records");
+  const int ns = persist_max_stages(max_cols, G, hd);
+  if (ns < 3) return no("not enough shared memory for the weight ring");
+  int xs = 0;
+  const size_t smem = persist_smem_bytes(max_cols, G, hd, ns, &xs);
+  const int grid = ctx->sm_count;
+  const bool gemma = false, qkn = c.qk_norm != 0;
+  std::vector<PPhase> plan;
+  for (auto &L : ctx->layers) {
+    auto gemv_phase = [&](const DevLinear &W, const float *x, const float *norm_w, float *y, const float *bias, int epi) {
+      PPhase p{};
+      p.kind = PH_GEMV;
+      p.g.w = W.w;
+      p.g.type = W.type;
+      p.g.rows = W.rows;
+      p.g.cols = W.cols;
+      p.g.tiles = (W.rows + 15) / 16;
+      p.g.nkb = W.cols / 256;
+      p.g.x = x;
+      p.g.norm_w = norm_w;
+      p.g.eps = c.epsilon;
+      p.g.y = y;
+      p.g.bias = bias;
+      p.g.epi = epi;
+      return p;
+    };
+    plan.push_back(gemv_phase(L.qkv, ctx->hidden, L.attn_norm, ctx->qkv, L.qkv_bias, EPI_STORE));
+    PPhase at{};
+    at.kind = PH_ATTN;
+    at.a.qkv = ctx->qkv;
+    at.a.k = L.k_cache;
+    at.a.v = L.v_cache;
+    at.a.out = ctx->att;
+    at.a.q_norm = L.q_norm;
+    at.a.k_norm = L.k_norm;
+    at.a.table = L.rope_table;
+    at.a.heads = ctx->heads_l;
+    at.a.kv_heads = ctx->kv_l;
+    at.a.hd = hd;
+    at.a.capacity = L.capacity;
+    at.a.window = L.window;
+    at.a.rot = gemma ? hd : (c.rotary_dim ? c.rotary_dim : hd);
+    at.a.mode = qkn ? 0 : c.rope_mode;
+    at.a.scale = c.attention_scale;
+    at.a.eps = c.epsilon;
+    plan.push_back(at);
+    plan.push_back(gemv_phase(L.o, ctx->att, nullptr, ctx->hidden, L.o_bias, EPI_ADD));
+    const int epi = !c.ffn_gate ? EPI_SILU : c.activation == 1 ? EPI_GLU_GELU : EPI_GLU_SILU;
+    plan.push_back(gemv_phase(L.gate_up, ctx->hidden, L.ffn_norm, ctx->act, nullptr, epi));
+    plan.push_back(gemv_phase(L.down, ctx->act, nullptr, ctx->hidden, nullptr, EPI_ADD));
+  }
+  {
+    PPhase p{};
+    p.kind = PH_GEMV;
+    p.g.w = ctx->lm.w;
+    p.g.type = ctx->lm.type;
+    p.g.rows = ctx->lm.rows;
+    p.g.cols = H;
+    p.g.tiles = (ctx->lm.rows + 15) / 16;
+    p.g.nkb = H / 256;
+    p.g.x = ctx->hidden;
+    p.g.norm_w = ctx->out_norm;
+    p.g.eps = c.epsilon;
+    p.g.y = ctx->logits;
+    p.g.epi = EPI_STORE;
+    p.g.argmax = 1;
+    plan.push_back(p);
+  }
+  PersistArgs &a = ctx->pargs;
+  a = PersistArgs{};
+  PPhase *d_plan = nullptr;
+  float *att_part = nullptr;
+  unsigned *att_ctr = nullptr, *bar = nullptr;
+  float2 *cand = nullptr;
+  int *status = nullptr, rc;
+  const int nsp_max = std::max(1, std::min(64, grid / ctx->kv_l));
+  if ((rc = ctx_alloc(ctx, (void **)&d_plan, plan.size() * sizeof(PPhase), "decode plan")) ||
+      (rc = ctx_alloc_t(ctx, &att_part, (size_t)ctx->kv_l * nsp_max * G * (hd + 4), "decode attention partials")) ||
+      (rc = ctx_alloc_t(ctx, &att_ctr, (size_t)ctx->kv_l, "decode attention counters")) ||
+      (rc = ctx_alloc_t(ctx, &cand, (size_t)grid, "decode candidates")) || (rc = ctx_alloc_t(ctx, &bar, 2, "grid barrier")) ||
+      (rc = ctx_alloc_t(ctx, &status, 4, "decode status")))
+    return rc;
+  CK(cudaMemcpy(d_plan, plan.data(), plan.size() * sizeof(PPhase), cudaMemcpyHostToDevice));
+  int *d_cancel = nullptr;
+  CK(cudaHostGetDevicePointer((void **)&d_cancel, ctx->h_io + IO_CANCEL, 0));
+  a.phases = d_plan;
+  a.nphases = (int)plan.size();
+  a.embd = ctx->embd.w;
+  a.embd_type = ctx->embd.type;
+  a.embd_tiled = ctx->embd.tiled ? 1 : 0;
+  a.embd_drow = ctx->embd.drow;
+  a.hidden = H;
+  a.vocab = c.vocab;
+  a.embd_scale = 1.f;
+  a.x = ctx->hidden;
+  a.tokens = ctx->d_tokens;
+  a.cancel = d_cancel;
+  a.att_part = att_part;
+  a.att_ctr = att_ctr;
+  a.cand = cand;
+  a.bar = bar;
+  a.status = status;
+  a.nstage = ns;
+  a.xs_bytes = xs;
+  a.nsp_max = nsp_max;
+  a.l2_ahead = 0;
+  if (const char *v = getenv("WGD_PERSIST_L2_AHEAD")) a.l2_ahead = std::max(0, std::min(64, atoi(v)));  // tuning override
+  (void)smem;
+  ctx->persist_ok = true;
+  ctx->persist_why = "";
+  return WGD_OK;
+}
+
+// Runs `steps` greedy tokens from (first, start) in one launch; the tokens land in
+// d_tokens and the status words in h_io[IO_STATUS..]. Stream-ordered (no sync).
+static int enqueue_persist(wgd_ctx *ctx, int first, int start, int steps) {
+  PersistArgs a = ctx->pargs;
+  a.first = first;
+  a.start = start;
+  a.steps = steps;
+  CK(cudaMemsetAsync(a.status, 0, 4 * sizeof(int), ctx->stream));
+  CK(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), ctx->stream));  // arrivals only; the generation word keeps counting
+  CK(launch_persist(a, ctx->sm_count, ctx->stream));
+  CK(cudaMemcpyAsync(ctx->h_io + IO_STATUS, a.status, 4 * sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+  ctx->kernels = 1;
+  ctx->st.kernel_launches += 1;
+  return WGD_OK;
+}
+
+// Maps the persistent kernel's status word to the API's errors.
+static int persist_status(wgd_ctx *ctx) {
+  switch (ctx->h_io[IO_STATUS]) {
+    case 0: return WGD_OK;
+    case 2: return fail(WGD_ENONFINITE, "Inference produced non-finite logits. Stop and report this model/runtime combination.");
+    case 3: return fail(WGD_ECANCELLED, "Stopped by user");
+    default: return fail(WGD_ETIMEOUT, "a wait inside the decode kernel ran past its limit");
+  }
+}
+
 extern "C" int wgd_model_end(wgd_ctx *ctx) {
   if (!ctx) return fail(WGD_EINVAL, "null context");
   if (!ctx->begun || ctx->ended) return fail(WGD_ESTATE, "model_end out of order");
@@ -576,6 +744,7 @@ extern "C" int wgd_model_end(wgd_ctx *ctx) {
   if (tp > 1) {
     if ((rc = tp_create(&ctx->tp, ctx->tp_rank, tp, (size_t)B * H, &g_err))) return rc;
   }
+  if ((rc = build_persist_plan(ctx))) return rc;
   ctx->ended = true;
   ctx->st.gpu_bytes = ctx->allocated;
   ctx->st.peak_gpu_bytes = ctx->peak;
@@ -857,7 +1026,12 @@ extern "C" int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, i
   CK(cudaEventRecord(ctx->ev0, ctx->stream));
   int rc;
   const bool gather_logits = want == 2;
-  if (n == 1 && ctx->graphs && !gather_logits) {
+  const bool persist = n == 1 && ctx->persist_ok && ctx->persist_on;
+  if (persist) {
+    ctx->h_io[IO_CANCEL] = 0;
+    if ((rc = enqueue_persist(ctx, ids[0], start, 1))) return rc;
+    CK(cudaMemcpyAsync(ctx->h_io + 1, ctx->d_tokens, sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream));
+  } else if (n == 1 && ctx->graphs && !gather_logits) {
     if (!ctx->decode_exec) {
       CK(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
       rc = enqueue_forward(ctx, 1, false);
@@ -867,10 +1041,14 @@ extern "C" int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, i
       if (e != cudaSuccess) return fail(WGD_ECUDA, std::string("graph capture: ") + cudaGetErrorString(e));
       ctx->decode_graph = g;
       CK(cudaGraphInstantiate(&ctx->decode_exec, g, 0));
+      ctx->decode_kernels = ctx->kernels;
     }
     CK(cudaGraphLaunch(ctx->decode_exec, ctx->stream));
+    ctx->kernels = ctx->decode_kernels;
+    ctx->st.kernel_launches += ctx->kernels;
   } else {
     if ((rc = enqueue_forward(ctx, n, gather_logits))) return rc;
+    ctx->st.kernel_launches += ctx->kernels;
   }
   CK(cudaEventRecord(ctx->ev1, ctx->stream));
   if (want == 2 && logits_out) {
@@ -883,6 +1061,7 @@ extern "C" int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, i
   ctx->st.forwards++;
   ctx->st.tokens += n;
   if (ctx->tp && tp_failed(ctx->tp)) return fail(WGD_ETIMEOUT, "a tensor-parallel peer did not answer within the wait limit");
+  if (persist && (rc = persist_status(ctx))) return rc;
   if (want >= 1) {
     if (ctx->h_io[1] < 0) return fail(WGD_ENONFINITE, "Inference produced non-finite logits. Stop and report this model/runtime combination.");
     if (argmax_out) *argmax_out = ctx->h_io[1];
@@ -900,6 +1079,21 @@ extern "C" int wgd_decode(wgd_ctx *ctx, int32_t first, int start, int steps, int
   if (ctx->cancel.exchange(0)) return fail(WGD_ECANCELLED, "Stopped by user");
   CK(cudaSetDevice(ctx->device));
   int rc;
+  if (ctx->persist_ok && ctx->persist_on) {
+    ctx->h_io[IO_CANCEL] = 0;
+    CK(cudaEventRecord(ctx->ev0, ctx->stream));
+    if ((rc = enqueue_persist(ctx, first, start, steps))) return rc;
+    CK(cudaEventRecord(ctx->ev1, ctx->stream));
+    CK(cudaMemcpyAsync(tokens_out, ctx->d_tokens, sizeof(int32_t) * steps, cudaMemcpyDeviceToHost, ctx->stream));
+    CK(cudaStreamSynchronize(ctx->stream));
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, ctx->ev0, ctx->ev1);
+    const int done = ctx->h_io[IO_STATUS + 1];
+    ctx->st.last_forward_ms = ms;
+    ctx->st.forwards += done;
+    ctx->st.tokens += done;
+    return persist_status(ctx);
+  }
   if (!ctx->chain_exec) {
     CK(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
     rc = enqueue_forward(ctx, 1, false, false);
@@ -914,7 +1108,10 @@ extern "C" int wgd_decode(wgd_ctx *ctx, int32_t first, int start, int steps, int
     if (e != cudaSuccess) return fail(WGD_ECUDA, std::string("graph capture: ") + cudaGetErrorString(e));
     ctx->chain_graph = g;
     CK(cudaGraphInstantiate(&ctx->chain_exec, g, 0));
+    ctx->chain_kernels = ctx->kernels;
   }
+  ctx->kernels = ctx->chain_kernels;
+  ctx->st.kernel_launches += (uint64_t)ctx->kernels * steps;
   ctx->h_io[0] = start;
   ctx->h_io[2] = first;
   ctx->h_io[3] = 0;
@@ -953,7 +1150,9 @@ extern "C" int wgd_truncate_kv(wgd_ctx *ctx, int n_tokens) {
 }
 
 extern "C" void wgd_cancel(wgd_ctx *ctx) {
-  if (ctx) ctx->cancel.store(1);
+  if (!ctx) return;
+  ctx->cancel.store(1);
+  if (ctx->h_io) reinterpret_cast<volatile int32_t *>(ctx->h_io)[IO_CANCEL] = 1;  // polled by a running decode kernel
 }
 
 extern "C" int wgd_stats_get(wgd_ctx *ctx, wgd_stats *out) {
@@ -968,6 +1167,18 @@ extern "C" int wgd_set_graphs(wgd_ctx *ctx, int enabled) {
   if (!ctx) return fail(WGD_EINVAL, "null context");
   ctx->graphs = enabled != 0;
   return WGD_OK;
+}
+
+extern "C" int wgd_set_persistent(wgd_ctx *ctx, int enabled) {
+  if (!ctx) return fail(WGD_EINVAL, "null context");
+  ctx->persist_on = enabled != 0;
+  return WGD_OK;
+}
+
+extern "C" int wgd_persistent_status(wgd_ctx *ctx, char *why, int why_len) {
+  if (!ctx) return fail(WGD_EINVAL, "null context");
+  if (why && why_len > 0) snprintf(why, (size_t)why_len, "%s", ctx->persist_why.c_str());
+  return ctx->persist_ok ? 1 : 0;
 }
 
 // ------------------------------------------------------------ tensor parallel

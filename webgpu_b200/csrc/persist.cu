@@ -1,0 +1,1109 @@
+// Persistent decode kernel (see persist.h). Per token it runs, for every
+// layer, the phases of PagedEngine.forward's denseLayer (engine.ts:217-251 of
+// the reference): RMSNorm+QKV projection (+bias), RoPE + KV ring write +
+// attention (attentionShader, shaders.ts:88-122), output projection +
+// residual, RMSNorm + gate|up projection + SwiGLU, down projection +
+// residual; then the final norm + LM head and the greedy argmax
+// (engine.ts:305-309), and feeds the token back to the embedding gather
+// (engine.ts:140-145).
+//
+// Synchronisation:
+//  * between phases, a grid barrier (all CTAs are co-resident: cooperative
+//    launch, one CTA per SM) with an arrival counter and a generation word;
+//  * inside a CTA, the producer warp and the consumer warps share a ring of
+//    shared-memory slots guarded by mbarriers ("full": transaction bytes of the
+//    bulk copy; "empty": one arrival per consumer warp);
+//  * a 16-row output tile whose units are spread over the CTA's warps is
+//    summed in warp order by the warp that publishes last; a tile cut between
+//    CTAs is finished by the CTA that arrives last, summing in CTA order, so
+//    every sum has a fixed order.
+// Every wait is bounded by a globaltimer deadline; a wait that runs out sets
+// status[0] = 1 and the whole grid winds down (the producer first waits for its
+// copies in flight).
+#include <float.h>
+
+#include "gemv2_impl.cuh"
+#include "kernels.h"
+#include "persist.h"
+#include "quant.cuh"
+#include "tile.cuh"
+
+namespace wgd {
+namespace {
+
+// ------------------------------------------------------------------ PTX helpers
+
+__device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t *b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t *b, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bulk copy global -> this CTA's shared memory, completing on mbarrier `bar`
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(su32(dst)),
+               "l"(src), "r"(bytes), "r"(su32(bar))
+               : "memory");
+}
+__device__ __forceinline__ uint64_t gtime() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void asyncb() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(unsigned *p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void *smem, const void *g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(su32(smem)), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+constexpr uint64_t P_TIMEOUT_NS = 2000000000ull;  // 2 s: far above any legitimate wait
+
+// Phase timeline for profiling builds (-DWGD_PERSIST_TRACE): globaltimer stamps of
+// CTAs 0 and 100 per (step, phase): [0] start, [1] input digitised, [2] last unit
+// computed, [3] finished; [4], [5] producer issue of the phase's first / last stage.
+#ifdef WGD_PERSIST_TRACE
+constexpr int TR_STEPS = 4, TR_PHASES = 256, TR_SLOTS = 8;
+__device__ uint64_t g_trace[2][TR_STEPS][TR_PHASES][TR_SLOTS];
+// every CTA's barrier arrival / release of step 1: [cta][barrier index][2]
+constexpr int TR_BARS = 256;
+__device__ uint64_t g_bars[160][TR_BARS][2];
+__device__ int g_bar_index[160];
+__device__ uint64_t g_wait_acc[2];  // ns thread 0 of CTAs 0 / 100 spent waiting for ring slots (per phase)
+#define P_TRACE(step, phase, slot)                                                                          \
+  do {                                                                                                     \
+    if ((blockIdx.x == 0 || blockIdx.x == 100) && (step) < TR_STEPS && (phase) < TR_PHASES)                \
+      g_trace[blockIdx.x == 0 ? 0 : 1][step][phase][slot] = gtime();                                       \
+  } while (0)
+#else
+#define P_TRACE(step, phase, slot) \
+  do {                             \
+  } while (0)
+#endif
+
+// Warp roles: 0..7 compute (digitise, tile-chunk math, attention, embedding), 8 epilogue
+// (sums each tile's chunk results in k-block order, stores, greedy tracking), 9 producer.
+constexpr int P_EWARP = P_CWARPS, P_PWARP = P_CWARPS + 1;
+constexpr int P_MAXSTAGES = 8, P_STAGE_UNITS = 16, P_RES_STAGES = 8;
+
+// Shared state of one CTA besides the ring and the xs region.
+struct PShared {
+  float res[P_RES_STAGES][P_STAGE_UNITS][16];  // per stage (mod P_RES_STAGES): the 16 row sums of each chunk
+  float red[P_CWARPS];
+  float2 best[P_CWARPS + 1];
+  int flags[4];  // [0] stop (finished / winding down), [1] attention last-arriver, [2] token, [3] stop snapshot
+};
+// compute + epilogue warps / compute warps only
+__device__ __forceinline__ void bar_all() { asm volatile("bar.sync 1, %0;" ::"n"((P_CWARPS + 1) * 32) : "memory"); }
+__device__ __forceinline__ void bar_comp() { asm volatile("bar.sync 3, %0;" ::"n"(P_CWARPS * 32) : "memory"); }
+
+__device__ __forceinline__ int chunk_bytes(int type) { return type == Q4_K ? 2304 : 3360; }
+__device__ __forceinline__ int slot_units(int type) { return P_SLOT_BYTES / chunk_bytes(type); }
+
+// CTA c owns whole output tiles [tiles*c/grid, tiles*(c+1)/grid): no tile is cut
+// between CTAs (at most one tile of imbalance, no cross-CTA reduction).
+__device__ __forceinline__ void unit_range(int tiles, int nkb, int grid, int c, int &u0, int &u1) {
+  u0 = (int)((long long)tiles * c / grid) * nkb;
+  u1 = (int)((long long)tiles * (c + 1) / grid) * nkb;
+}
+
+// better(a, b): a is a finite logit with a higher value, or equal value and lower index
+__device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
+  if (ia < 0) return false;
+  if (ib < 0) return true;
+  return va > vb || (va == vb && ia < ib);
+}
+
+// ------------------------------------------------------------------ GEMV pieces
+
+// Digit records of the phase input in shared memory (one activation row), laid
+// out so that the 16-byte loads of a warp hit distinct bank groups: per 256-column
+// super-block sb,
+//   brec sb*960 + (dg*4 + tig)*80 + j*8 + hi*4   digit plane dg at k = 4tig.. (hi 0) /
+//                                                16+4tig.. (hi 1) of 32-block j
+//   ds   Q4_K: sb*320 + tig*80 + j*8 + pos*4     digit sum over 32-block j of MMA column 2tig+pos
+//        Q6_K: sb*576 + tig*144 + r*8 + pos*4    the same over 16-run r
+//   sxs[sb]                                      digit scale
+// (records 80 bytes apart: 12 live records fall on 8 bank groups, two wavefronts).
+struct PX {
+  uint8_t *brec, *ds;
+  float *sxs;
+};
+__host__ __device__ inline size_t px_bytes(int cols) {
+  const size_t nsb = (size_t)cols / 256;
+  return nsb * 960 + nsb * 576 + nsb * 4 + 64;
+}
+__device__ __forceinline__ PX px_carve(uint8_t *xs, int cols) {
+  const int nsb = cols >> 8;
+  PX X;
+  X.brec = xs;
+  X.ds = xs + (size_t)nsb * 960;
+  X.sxs = reinterpret_cast<float *>(X.ds + (size_t)nsb * 576);
+  return X;
+}
+constexpr int P_MAXSBW = 4;  // super-blocks per compute warp: inputs up to 16*4*256 = 16384 wide
+static_assert(P_CWARPS == 16, "digit records assume 16 compute warps");
+
+// Lane constants: the lane's B record (dead MMA columns 3..7 reuse plane 0 and get weight 0)
+// and the digit weights of its two D columns n0 = 2tig, n1 = 2tig + 1.
+struct PLane {
+  uint32_t boff;
+  float w0, w1;
+  int tig;
+};
+__device__ __forceinline__ PLane p_lane(int lane) {
+  const int grp = lane >> 2, tig = lane & 3, dg = grp < 3 ? grp : 0;
+  PLane L;
+  L.boff = (uint32_t)(dg * 4 + tig) * 80;
+  L.w0 = tig == 0 ? 1.f : tig == 1 ? 1.f / 64516.f : 0.f;
+  L.w1 = tig == 0 ? 1.f / 254.f : 0.f;
+  L.tig = tig;
+  return L;
+}
+
+// Digitise the phase input (RMS-normalised when nw is set) with one round of L2
+// loads: warp w holds super-blocks w, w+16, ... in registers, the norm's sum of
+// squares comes from the same registers. x ~= s * (a + b/254 + c/254^2), s =
+// max|x|/127 per super-block (the same digits as the stand-alone GEMV).
+__device__ void p_digitise(const float *x, const float *nw, float eps, int cols, bool q6, const PX &X, float *red, int warp,
+                           int lane) {
+  const int nsb = cols >> 8;
+  const int q8 = lane & 7, tg = q8 & 3, hi = q8 >> 2;
+  float4 v[P_MAXSBW][2];
+#pragma unroll
+  for (int i = 0; i < P_MAXSBW; i++) {
+    const int sb = warp + P_CWARPS * i;
+#pragma unroll
+    for (int p = 0; p < 2; p++) {
+      const int col = 256 * sb + 32 * ((lane >> 3) + 4 * p) + 4 * q8;
+      const bool in = sb < nsb;
+      v[i][p] = in ? __ldcg(reinterpret_cast<const float4 *>(x + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      // the norm weights are read after the block-wide sum: bring them into L1 now
+      if (in && nw) asm volatile("prefetch.global.L1 [%0];" ::"l"(nw + col));
+    }
+  }
+  if (nw) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < P_MAXSBW; i++)
+#pragma unroll
+      for (int p = 0; p < 2; p++)
+        ss = fmaf(v[i][p].x, v[i][p].x, fmaf(v[i][p].y, v[i][p].y, fmaf(v[i][p].z, v[i][p].z, fmaf(v[i][p].w, v[i][p].w, ss))));
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    bar_comp();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < P_CWARPS; w++) t += red[w];
+    const float inv = rsqrtf(t / (float)cols + eps);
+#pragma unroll
+    for (int i = 0; i < P_MAXSBW; i++) {
+      const int sb = warp + P_CWARPS * i;
+      if (sb >= nsb) continue;
+#pragma unroll
+      for (int p = 0; p < 2; p++) {
+        const int col = 256 * sb + 32 * ((lane >> 3) + 4 * p) + 4 * q8;
+        const float4 w = __ldg(reinterpret_cast<const float4 *>(nw + col));
+        v[i][p] = make_float4(v[i][p].x * inv * w.x, v[i][p].y * inv * w.y, v[i][p].z * inv * w.z, v[i][p].w * inv * w.w);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < P_MAXSBW; i++) {
+    const int sb = warp + P_CWARPS * i;
+    if (sb >= nsb) continue;
+    float amax = 0.f;
+#pragma unroll
+    for (int p = 0; p < 2; p++)
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i][p].x), fabsf(v[i][p].y)), fmaxf(fabsf(v[i][p].z), fabsf(v[i][p].w))));
+    amax = warp_max(amax);
+    const float sc = amax > 0.f ? 127.f / amax : 0.f;
+    if (lane == 0) X.sxs[sb] = amax > 0.f ? amax / 127.f : 0.f;
+#pragma unroll
+    for (int p = 0; p < 2; p++) {
+      const int j = (lane >> 3) + 4 * p;
+      const float xs4[4] = {v[i][p].x, v[i][p].y, v[i][p].z, v[i][p].w};
+      uint32_t pk[3] = {0u, 0u, 0u};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float t = xs4[e] * sc;
+        const float fa = rintf(t), r1 = (t - fa) * 254.f;
+        const float fb = rintf(r1), r2 = (r1 - fb) * 254.f;
+        const float fc = rintf(r2);
+        pk[0] |= ((uint32_t)(int)fa & 255u) << (8 * e);
+        pk[1] |= ((uint32_t)(int)fb & 255u) << (8 * e);
+        pk[2] |= ((uint32_t)(int)fc & 255u) << (8 * e);
+      }
+#pragma unroll
+      for (int dg = 0; dg < 3; dg++) {
+        *reinterpret_cast<uint32_t *>(X.brec + (size_t)sb * 960 + (dg * 4 + tg) * 80 + j * 8 + hi * 4) = pk[dg];
+        int s16 = __dp4a((int)pk[dg], 0x01010101, 0);  // this quad's digit sum
+        s16 += __shfl_xor_sync(0xffffffffu, s16, 1);
+        s16 += __shfl_xor_sync(0xffffffffu, s16, 2);   // 16-run 2j + hi
+        const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 4);  // 32-block j
+        const int tgn = dg >> 1, pos = dg & 1;          // MMA column dg sits at tig dg/2, component dg%2
+        if (q6) {
+          if ((q8 & 3) == 0) *reinterpret_cast<int *>(X.ds + (size_t)sb * 576 + tgn * 144 + (2 * j + hi) * 8 + pos * 4) = s16;
+        } else if (q8 == 0) {
+          *reinterpret_cast<int *>(X.ds + (size_t)sb * 320 + tgn * 80 + j * 8 + pos * 4) = s32;
+        }
+      }
+    }
+  }
+}
+
+// One Q4_K tile chunk (16 rows x 256 columns, staged in shared memory at c) against the
+// digit records of super-block kb: the integer formulation of gemv2_impl.cuh.
+__device__ __forceinline__ void p_q4k(const uint8_t *c, int kb, const PX &X, const PLane &P, int lane, float (&acc)[2]) {
+  Q4KRegs r;
+#pragma unroll
+  for (int g = 0; g < 4; g++) r.qs[g] = *reinterpret_cast<const uint4 *>(c + 512 * g + 16 * lane);
+  const int grp = lane >> 2;
+  r.h0 = *reinterpret_cast<const uint4 *>(c + 2048 + 16 * grp);
+  r.h1 = *reinterpret_cast<const uint4 *>(c + 2048 + 16 * (grp + 8));
+  const uint32_t M4 = 0x0F0F0F0Fu;
+  const uint32_t sc_lo0 = r.h0.y & 0x3F3F3F3Fu, mn_lo0 = r.h0.z & 0x3F3F3F3Fu;
+  const uint32_t sc_hi0 = (r.h0.w & M4) | ((r.h0.y >> 2) & 0x30303030u);
+  const uint32_t mn_hi0 = ((r.h0.w >> 4) & M4) | ((r.h0.z >> 2) & 0x30303030u);
+  const uint32_t sc_lo1 = r.h1.y & 0x3F3F3F3Fu, mn_lo1 = r.h1.z & 0x3F3F3F3Fu;
+  const uint32_t sc_hi1 = (r.h1.w & M4) | ((r.h1.y >> 2) & 0x30303030u);
+  const uint32_t mn_hi1 = ((r.h1.w >> 4) & M4) | ((r.h1.z >> 2) & 0x30303030u);
+  const uint4 *bp = reinterpret_cast<const uint4 *>(X.brec + (size_t)kb * 960 + P.boff);
+  const int4 *dp = reinterpret_cast<const int4 *>(X.ds + (size_t)kb * 320 + P.tig * 80);
+  uint4 B[4];
+  int4 DS[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) { B[i] = bp[i]; DS[i] = dp[i]; }
+  int I00 = 0, I01 = 0, I10 = 0, I11 = 0, M00 = 0, M01 = 0, M10 = 0, M11 = 0;
+#pragma unroll
+  for (int g = 0; g < 4; g++) {
+    const uint32_t w[4] = {r.qs[g].x, r.qs[g].y, r.qs[g].z, r.qs[g].w};
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+      const int s = 2 * g + half;
+      const uint32_t aa[4] = {half ? (w[0] >> 4) & M4 : w[0] & M4, half ? (w[1] >> 4) & M4 : w[1] & M4,
+                              half ? (w[2] >> 4) & M4 : w[2] & M4, half ? (w[3] >> 4) & M4 : w[3] & M4};
+      const int sc0 = ubyte(s < 4 ? sc_lo0 : sc_hi0, s & 3), mn0 = ubyte(s < 4 ? mn_lo0 : mn_hi0, s & 3);
+      const int sc1 = ubyte(s < 4 ? sc_lo1 : sc_hi1, s & 3), mn1 = ubyte(s < 4 ? mn_lo1 : mn_hi1, s & 3);
+      const uint4 bq = B[s >> 1];
+      int D[4];
+      mma_k32(D, aa, (s & 1) ? bq.z : bq.x, (s & 1) ? bq.w : bq.y);
+      const int4 dq = DS[s >> 1];
+      const int dx = (s & 1) ? dq.z : dq.x, dy = (s & 1) ? dq.w : dq.y;
+      // |D| <= 32*15*127 = 60960; x sc <= 63 and 8 sub-blocks: < 3.1e7. |dsum| <= 4064; x mn x 8 < 2.1e6.
+      I00 += sc0 * D[0];
+      I01 += sc0 * D[1];
+      I10 += sc1 * D[2];
+      I11 += sc1 * D[3];
+      M00 += mn0 * dx;
+      M01 += mn0 * dy;
+      M10 += mn1 * dx;
+      M11 += mn1 * dy;
+    }
+  }
+  const float d0 = h2f(r.h0.x), d1 = h2f(r.h1.x), m0 = h2f(r.h0.x >> 16), m1 = h2f(r.h1.x >> 16);
+  const float sx = X.sxs[kb];
+  acc[0] = fmaf(sx, fmaf(P.w0, d0 * (float)I00 - m0 * (float)M00, P.w1 * (d0 * (float)I01 - m0 * (float)M01)), acc[0]);
+  acc[1] = fmaf(sx, fmaf(P.w0, d1 * (float)I10 - m1 * (float)M10, P.w1 * (d1 * (float)I11 - m1 * (float)M11)), acc[1]);
+}
+
+__device__ __forceinline__ void p_q6k(const uint8_t *c, int kb, const PX &X, const PLane &P, int lane, float (&acc)[2]) {
+  Q6KRegs r;
+#pragma unroll
+  for (int k = 0; k < 4; k++) r.ql[k] = *reinterpret_cast<const uint4 *>(c + 512 * k + 16 * lane);
+  r.qh[0] = *reinterpret_cast<const uint4 *>(c + 2048 + 16 * lane);
+  r.qh[1] = *reinterpret_cast<const uint4 *>(c + 2560 + 16 * lane);
+  const int grp = lane >> 2;
+  r.s0 = *reinterpret_cast<const uint4 *>(c + 3072 + 16 * grp);
+  r.s1 = *reinterpret_cast<const uint4 *>(c + 3072 + 16 * (grp + 8));
+  r.d = (uint32_t)*reinterpret_cast<const uint16_t *>(c + 3328 + 2 * grp) |
+        ((uint32_t)*reinterpret_cast<const uint16_t *>(c + 3328 + 2 * (grp + 8)) << 16);
+  const uint32_t M4 = 0x0F0F0F0Fu, T3 = 0x03030303u;
+  const uint32_t sw0[4] = {r.s0.x, r.s0.y, r.s0.z, r.s0.w}, sw1[4] = {r.s1.x, r.s1.y, r.s1.z, r.s1.w};
+  const uint4 *bp = reinterpret_cast<const uint4 *>(X.brec + (size_t)kb * 960 + P.boff);
+  const int4 *dsp = reinterpret_cast<const int4 *>(X.ds + (size_t)kb * 576 + P.tig * 144);
+  uint4 B[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) B[i] = bp[i];
+  int I00 = 0, I01 = 0, I10 = 0, I11 = 0;
+#pragma unroll
+  for (int seg = 0; seg < 2; seg++) {
+    const uint32_t hw[4] = {r.qh[seg].x, r.qh[seg].y, r.qh[seg].z, r.qh[seg].w};
+#pragma unroll
+    for (int quarter = 0; quarter < 4; quarter++) {
+      const int qp = quarter & 1, nib = quarter >> 1;
+      const uint4 lw = r.ql[2 * seg + qp];
+      const uint32_t l[4] = {lw.x, lw.y, lw.z, lw.w};
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int s = 8 * seg + 2 * quarter + h;  // sub-block of 16 values; 32-block s/2, half h
+        const uint32_t a0 = ((l[2 * h] >> (4 * nib)) & M4) | (((hw[2 * h] >> (2 * quarter)) & T3) << 4);
+        const uint32_t a1 = ((l[2 * h + 1] >> (4 * nib)) & M4) | (((hw[2 * h + 1] >> (2 * quarter)) & T3) << 4);
+        const int sc0 = sbyte(sw0[s >> 2], s & 3), sc1 = sbyte(sw1[s >> 2], s & 3);
+        const uint4 bq = B[s >> 2];
+        const int j = s >> 1;
+        const uint32_t b0 = (j & 1) ? (h ? bq.w : bq.z) : (h ? bq.y : bq.x);
+        int D[4];
+        mma_k16(D, a0, a1, b0);
+        const int4 dq = dsp[s >> 1];
+        const int dx = (s & 1) ? dq.z : dq.x, dy = (s & 1) ? dq.w : dq.y;
+        // |D - 32*dsum| <= 16*32*127 = 65024; x |sc| <= 128 and 16 sub-blocks: < 1.4e8.
+        I00 += sc0 * (D[0] - 32 * dx);
+        I01 += sc0 * (D[1] - 32 * dy);
+        I10 += sc1 * (D[2] - 32 * dx);
+        I11 += sc1 * (D[3] - 32 * dy);
+      }
+    }
+  }
+  const float d0 = h2f(r.d), d1 = h2f(r.d >> 16);
+  const float sx = X.sxs[kb];
+  acc[0] = fmaf(sx, fmaf(P.w0, d0 * (float)I00, P.w1 * (d0 * (float)I01)), acc[0]);
+  acc[1] = fmaf(sx, fmaf(P.w0, d1 * (float)I10, P.w1 * (d1 * (float)I11)), acc[1]);
+}
+
+struct GemvCtx {
+  const PGemv *g;
+  float best_v;  // greedy tracking (per lane)
+  int best_i;
+};
+
+// Epilogue of one finished tile: lane r < 16 holds the value of tile row r.
+__device__ __forceinline__ void p_epilogue(GemvCtx &C, int t, float v, int lane) {
+  const PGemv &g = *C.g;
+  if (g.epi == EPI_GLU_SILU || g.epi == EPI_GLU_GELU) {
+    const float up = __shfl_sync(0xffffffffu, v, (lane + 8) & 31);
+    if (lane < 8 && t * 16 + lane < g.rows) g.y[t * 8 + lane] = (g.epi == EPI_GLU_SILU ? g2_silu(v) : g2_gelu(v)) * up;
+    return;
+  }
+  const int row = t * 16 + lane;
+  if (lane < 16 && row < g.rows) {
+    float val = v;
+    if (g.bias) val += __ldg(g.bias + row);
+    if (g.epi == EPI_ADD) {
+      val = __ldcg(g.y + row) + val;
+      g.y[row] = val;
+    } else if (g.epi == EPI_SILU) {
+      val = g2_silu(val);
+      g.y[row] = val;
+    } else {
+      g.y[row] = val;
+    }
+    if (g.argmax && isfinite(val) && better(val, row, C.best_v, C.best_i)) {
+      C.best_v = val;
+      C.best_i = row;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ attention item
+
+// One (kv head, key split) of decode attention by consumer warps 0..3 (128
+// threads, named barrier 2); same math and merge order as attention_kernel.
+// Shared memory of one attention item (floats): [K|V stage 1][K|V stage 0][q][new k][new v],
+// a stage holding 32 rows of hd + 4 floats each for K and V.
+__device__ __forceinline__ int attn_stage_floats(int hd) { return 2 * 32 * (hd + 4); }
+__device__ __forceinline__ float *attn_stage(float *sm, int hd, int st) { return sm + (st ? 0 : attn_stage_floats(hd)); }
+
+// Issue the cp.async copies of K/V rows [tile, min(tile + 32, p1)) of kv head kh into stage st
+// (the row of the position being decoded comes from shared memory instead) and commit them.
+__device__ void p_attn_stage(const PAttn &A, int pos, int kh, int p1, int tile, float *sm, int st, int tid) {
+  const int hd = A.hd, hd4 = hd >> 2, RS = hd + 4, end = pos + 1;
+  const bool owns_new = p1 == end;
+  const float *kb = A.k + (int64_t)kh * A.capacity * hd, *vb = A.v + (int64_t)kh * A.capacity * hd;
+  const int cnt = min(32, p1 - tile), total = cnt * hd4;
+  float *ks = attn_stage(sm, hd, st), *vs = ks + 32 * RS;
+  for (int i = tid; i < total; i += 128) {
+    const int r = i / hd4, c = (i - r * hd4) * 4;
+    const int p = tile + r;
+    if (owns_new && p == end - 1) continue;
+    const int64_t row = (int64_t)(p % A.capacity) * hd;
+    cp_async16(ks + r * RS + c, kb + row + c);
+    cp_async16(vs + r * RS + c, vb + row + c);
+  }
+  cp_commit();
+}
+
+// Key split of the item: positions [p0, p1).
+__device__ __forceinline__ void attn_split(const PAttn &A, int pos, int nspmax, int &chunk, int &nsp) {
+  const int end = pos + 1, L = end < A.window ? end : A.window;
+  chunk = (L + nspmax - 1) / nspmax;
+  if (chunk < 32) chunk = 32;
+  nsp = (L + chunk - 1) / chunk;
+}
+
+// One (kv head, key split) of decode attention by consumer warps 0..3 (128 threads,
+// named barrier 2). `staged`: stage 0 already holds the first K/V tile (issued while
+// the QKV projection ran).
+__device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, int chunk, int nspmax, float *sm, float *att_part,
+                            unsigned *att_ctr, int *last_s, bool staged) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = A.heads / A.kv_heads, hd = A.hd, hd4 = hd >> 2, RS = hd + 4;
+  float *q_s = sm + 2 * attn_stage_floats(hd), *kn_s = q_s + G * hd, *vn_s = kn_s + hd;
+  const int end = pos + 1, begin = end - (end < A.window ? end : A.window);
+  const int p0 = begin + sp * chunk, p1 = min(end, p0 + chunk);
+  const bool owns_new = p1 == end;
+  const int ntiles = (p1 - p0 + 31) / 32;
+  if (!staged) p_attn_stage(A, pos, kh, p1, p0, sm, 0, tid);
+  if (ntiles > 1) p_attn_stage(A, pos, kh, p1, p0 + 32, sm, 1, tid);
+  const int hq = G + (owns_new ? 1 : 0);
+  for (int i = tid; i < hq * hd; i += 128) {
+    const int g = i / hd, d = i - g * hd;
+    const float *src = g < G ? A.qkv + (int64_t)(kh * G + g) * hd : A.qkv + (int64_t)(A.heads + kh) * hd;
+    (g < G ? q_s + g * hd : kn_s)[d] = __ldcg(src + d);
+  }
+  if (owns_new)
+    for (int d = tid; d < hd; d += 128) vn_s[d] = __ldcg(A.qkv + (int64_t)(A.heads + A.kv_heads + kh) * hd + d);
+  asyncb();
+  for (int g = warp; g < hq; g += 4) {
+    float *hv = g < G ? q_s + g * hd : kn_s;
+    const float *nw = g < G ? A.q_norm : A.k_norm;
+    if (nw) {
+      float ss = 0.f;
+      for (int d = lane; d < hd; d += 32) ss = fmaf(hv[d], hv[d], ss);
+      const float inv = rsqrtf(warp_sum(ss) / (float)hd + A.eps);
+      __syncwarp();
+      for (int d = lane; d < hd; d += 32) hv[d] = hv[d] * inv * nw[d];
+      __syncwarp();
+    }
+    const int half = A.rot / 2;
+    const float2 *tb = A.table + (int64_t)pos * half;
+    for (int i = lane; i < half; i += 32) {
+      const float2 cs = __ldg(tb + i);
+      const int ia = A.mode == 0 ? i : 2 * i, ib = A.mode == 0 ? i + half : 2 * i + 1;
+      const float l = hv[ia], r = hv[ib];
+      hv[ia] = l * cs.x - r * cs.y;
+      hv[ib] = l * cs.y + r * cs.x;
+    }
+    __syncwarp();
+  }
+  asyncb();
+  if (owns_new) {
+    const int slot = pos % A.capacity;
+    float *kd = A.k + ((int64_t)kh * A.capacity + slot) * hd, *vd = A.v + ((int64_t)kh * A.capacity + slot) * hd;
+    for (int d = tid; d < hd; d += 128) { kd[d] = kn_s[d]; vd[d] = vn_s[d]; }
+  }
+  const int g0 = warp, g1 = warp + 4;
+  const bool h0 = g0 < G, h1 = g1 < G;
+  float m0 = -FLT_MAX, m1 = -FLT_MAX, l0 = 0.f, l1 = 0.f;
+  float4 acc0[2], acc1[2];
+#pragma unroll
+  for (int i = 0; i < 2; i++) acc0[i] = acc1[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int ti = 0; ti < ntiles; ti++) {
+    const int tile = p0 + ti * 32, cnt = min(32, p1 - tile), st = ti & 1;
+    if (ti + 1 < ntiles) cp_wait<1>(); else cp_wait<0>();
+    asyncb();
+    float *ks = attn_stage(sm, hd, st), *vs = ks + 32 * RS;
+    if (owns_new && tile + cnt == end) {
+      const int r = end - 1 - tile;
+      for (int d = tid; d < hd; d += 128) { ks[r * RS + d] = kn_s[d]; vs[r * RS + d] = vn_s[d]; }
+      asyncb();
+    }
+    const bool live = lane < cnt;
+    float s0 = 0.f, s1 = 0.f;
+    {
+      const float4 *kr = reinterpret_cast<const float4 *>(ks + lane * RS);
+      const float4 *q0 = reinterpret_cast<const float4 *>(q_s + g0 * hd);
+      const float4 *q1 = reinterpret_cast<const float4 *>(q_s + (h1 ? g1 : g0) * hd);
+#pragma unroll 8
+      for (int d4 = 0; d4 < hd4; d4++) {
+        const float4 k4 = kr[d4];
+        if (h0) {
+          const float4 q = q0[d4];
+          s0 = fmaf(q.x, k4.x, fmaf(q.y, k4.y, fmaf(q.z, k4.z, fmaf(q.w, k4.w, s0))));
+        }
+        if (h1) {
+          const float4 q = q1[d4];
+          s1 = fmaf(q.x, k4.x, fmaf(q.y, k4.y, fmaf(q.z, k4.z, fmaf(q.w, k4.w, s1))));
+        }
+      }
+    }
+    float e0 = 0.f, e1 = 0.f;
+    if (h0) {
+      s0 = live ? s0 * A.scale : -FLT_MAX;
+      const float mn = fmaxf(m0, warp_max(s0)), corr = expf(m0 - mn);
+      e0 = live ? expf(s0 - mn) : 0.f;
+      l0 = fmaf(l0, corr, warp_sum(e0));
+      m0 = mn;
+#pragma unroll
+      for (int i = 0; i < 2; i++) acc0[i] = make_float4(acc0[i].x * corr, acc0[i].y * corr, acc0[i].z * corr, acc0[i].w * corr);
+    }
+    if (h1) {
+      s1 = live ? s1 * A.scale : -FLT_MAX;
+      const float mn = fmaxf(m1, warp_max(s1)), corr = expf(m1 - mn);
+      e1 = live ? expf(s1 - mn) : 0.f;
+      l1 = fmaf(l1, corr, warp_sum(e1));
+      m1 = mn;
+#pragma unroll
+      for (int i = 0; i < 2; i++) acc1[i] = make_float4(acc1[i].x * corr, acc1[i].y * corr, acc1[i].z * corr, acc1[i].w * corr);
+    }
+    if (h0) {
+#pragma unroll 4
+      for (int j = 0; j < cnt; j++) {
+        const float w0 = __shfl_sync(0xffffffffu, e0, j), w1 = __shfl_sync(0xffffffffu, e1, j);
+        const float4 *vr = reinterpret_cast<const float4 *>(vs + j * RS);
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+          const int d4 = lane + 32 * i;
+          if (d4 < hd4) {
+            const float4 v = vr[d4];
+            acc0[i] = make_float4(fmaf(w0, v.x, acc0[i].x), fmaf(w0, v.y, acc0[i].y), fmaf(w0, v.z, acc0[i].z), fmaf(w0, v.w, acc0[i].w));
+            if (h1)
+              acc1[i] = make_float4(fmaf(w1, v.x, acc1[i].x), fmaf(w1, v.y, acc1[i].y), fmaf(w1, v.z, acc1[i].z), fmaf(w1, v.w, acc1[i].w));
+          }
+        }
+      }
+    }
+    asyncb();
+    if (ti + 2 < ntiles) p_attn_stage(A, pos, kh, p1, tile + 64, sm, st, tid);
+  }
+  float *out_base = A.out + (int64_t)kh * G * hd;
+  if (nsp == 1) {
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const int d4 = lane + 32 * i;
+      if (d4 < hd4) {
+        if (h0) reinterpret_cast<float4 *>(out_base + g0 * hd)[d4] = make_float4(acc0[i].x / l0, acc0[i].y / l0, acc0[i].z / l0, acc0[i].w / l0);
+        if (h1) reinterpret_cast<float4 *>(out_base + g1 * hd)[d4] = make_float4(acc1[i].x / l1, acc1[i].y / l1, acc1[i].z / l1, acc1[i].w / l1);
+      }
+    }
+    return;
+  }
+  const int PR = hd + 4;
+  float *part = att_part + ((int64_t)kh * nspmax + sp) * G * PR;
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    const int d4 = lane + 32 * i;
+    if (d4 < hd4) {
+      if (h0) __stcg(reinterpret_cast<float4 *>(part + g0 * PR) + d4, acc0[i]);
+      if (h1) __stcg(reinterpret_cast<float4 *>(part + g1 * PR) + d4, acc1[i]);
+    }
+  }
+  if (lane == 0) {
+    if (h0) { __stcg(part + g0 * PR + hd, m0); __stcg(part + g0 * PR + hd + 1, l0); }
+    if (h1) { __stcg(part + g1 * PR + hd, m1); __stcg(part + g1 * PR + hd + 1, l1); }
+  }
+  __threadfence();
+  asyncb();
+  if (tid == 0) *last_s = atomicAdd(att_ctr + kh, 1u) == (unsigned)(nsp - 1);
+  asyncb();
+  if (!*last_s) return;
+  __threadfence();
+  const float *pb = att_part + (int64_t)kh * nspmax * G * PR;
+  const int64_t sstride = (int64_t)G * PR;
+  for (int g = warp; g < G; g += 4) {
+    const float *ph = pb + g * PR;
+    const float ma = lane < nsp ? __ldcg(ph + lane * sstride + hd) : -FLT_MAX;
+    const float mb = lane + 32 < nsp ? __ldcg(ph + (lane + 32) * sstride + hd) : -FLT_MAX;
+    const float M = warp_max(fmaxf(ma, mb));
+    const float wa = lane < nsp ? expf(ma - M) : 0.f, wb = lane + 32 < nsp ? expf(mb - M) : 0.f;
+    const float la = lane < nsp ? __ldcg(ph + lane * sstride + hd + 1) : 0.f;
+    const float lb = lane + 32 < nsp ? __ldcg(ph + (lane + 32) * sstride + hd + 1) : 0.f;
+    const float den = warp_sum(fmaf(wa, la, wb * lb));
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const int d4 = lane + 32 * i;
+      float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+      for (int j = 0; j < nsp; j++) {
+        const float w = __shfl_sync(0xffffffffu, j < 32 ? wa : wb, j & 31);
+        if (d4 < hd4) {
+          const float4 pv = __ldcg(reinterpret_cast<const float4 *>(ph + j * sstride) + d4);
+          num = make_float4(fmaf(w, pv.x, num.x), fmaf(w, pv.y, num.y), fmaf(w, pv.z, num.z), fmaf(w, pv.w, num.w));
+        }
+      }
+      if (d4 < hd4) reinterpret_cast<float4 *>(out_base + g * hd)[d4] = make_float4(num.x / den, num.y / den, num.z / den, num.w / den);
+    }
+  }
+  if (tid == 0) att_ctr[kh] = 0u;
+}
+
+// ------------------------------------------------------------------ embedding
+
+template <int T>
+__device__ __forceinline__ float p_embed_elem(const PersistArgs &a, int token, int col) {
+  if (a.embd_tiled) {
+    if constexpr (T == Q4_K || T == Q6_K) return dequant_tiled<T>(a.embd, a.hidden / 256, token, col);
+    return 0.f;
+  }
+  return dequant_elem<T>(a.embd + (int64_t)token * a.embd_drow, a.hidden / block_elems_dev<T>(), col);
+}
+__device__ float p_embed_value(const PersistArgs &a, int token, int col) {
+  switch (a.embd_type) {
+    case F32: return p_embed_elem<F32>(a, token, col);
+    case F16: return p_embed_elem<F16>(a, token, col);
+    case Q4_0: return p_embed_elem<Q4_0>(a, token, col);
+    case Q8_0: return p_embed_elem<Q8_0>(a, token, col);
+    case Q4_K: return p_embed_elem<Q4_K>(a, token, col);
+    case Q5_K: return p_embed_elem<Q5_K>(a, token, col);
+    default: return p_embed_elem<Q6_K>(a, token, col);
+  }
+}
+
+// ------------------------------------------------------------------ kernel
+
+struct Ring {
+  uint64_t *full, *empty;    // weight slots: bytes landed / compute warps done with them
+  uint64_t *done, *resfree;  // chunk results (P_RES_STAGES): written by the compute warps / read by the epilogue warp
+  uint8_t *slots;
+  int ns;
+};
+
+// Waits for phase `par` of mbarrier b. False when the grid is winding down or this
+// wait ran out (then status[0] = 1 and the stop flag is raised).
+__device__ bool mbar_wait(uint64_t *b, unsigned par, volatile int *stop, int *status) {
+  if (mbar_test(b, par)) return true;
+  const uint64_t t0 = gtime();
+#ifdef WGD_PERSIST_TRACE
+  struct Acc {
+    uint64_t t0;
+    __device__ ~Acc() {
+      if (threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == 100)) g_wait_acc[blockIdx.x == 0 ? 0 : 1] += gtime() - t0;
+    }
+  } acc_guard{t0};
+#endif
+  while (!mbar_test(b, par)) {
+    if (*stop) return false;
+    if (gtime() - t0 > P_TIMEOUT_NS) {
+      atomicCAS(status, 0, 1);
+      *stop = 1;
+      return false;
+    }
+    __nanosleep(32);
+  }
+  return true;
+}
+
+// Grid barrier for the compute and epilogue warps of every CTA. Returns false when
+// the grid is winding down. Every such warp reaches every call, also after a failed
+// wait, so no named barrier is left waiting.
+__device__ bool grid_sync(const PersistArgs &a, unsigned &gen, volatile int *stop) {
+  bar_all();
+#ifdef WGD_PERSIST_TRACE
+  int tr_i = -1;
+  if (threadIdx.x == 0 && blockIdx.x < 160) {
+    tr_i = g_bar_index[blockIdx.x]++;
+    if (tr_i >= 0 && tr_i < TR_BARS) g_bars[blockIdx.x][tr_i][0] = gtime();
+  }
+#endif
+  if (threadIdx.x == 0 && !*stop) {
+    // the CTA's writes are ordered before thread 0's release by the barrier above
+    const unsigned g = gen;
+    unsigned prev;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.bar) : "memory");
+    if (prev == gridDim.x - 1) {
+      asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(a.bar), "r"(0u) : "memory");
+      st_release(a.bar + 1, g + 1);
+    } else {
+      const uint64_t t0 = gtime();
+      for (unsigned it = 1; ld_acquire(a.bar + 1) == g; it++) {
+        if ((it & 63) == 0 && (*(volatile int *)a.status == 1 || gtime() - t0 > P_TIMEOUT_NS)) {
+          atomicCAS(a.status, 0, 1);
+          *stop = 1;
+          break;
+        }
+      }
+    }
+    gen = g + 1;
+  }
+#ifdef WGD_PERSIST_TRACE
+  if (threadIdx.x == 0 && tr_i >= 0 && tr_i < TR_BARS) g_bars[blockIdx.x][tr_i][1] = gtime();
+#endif
+  // one snapshot of the stop flag (the producer may raise it at any time) so that
+  // every thread takes the same branch after this barrier
+  if (threadIdx.x == 0) stop[3] = *stop;
+  bar_all();
+  return !stop[3];
+}
+
+// Cursor over the ring stages of this CTA, in execution order: (step, GEMV phase, first unit).
+struct SIt {
+  int step, p, u0, s0, u1, k, CB;
+  const uint8_t *w;
+};
+__device__ bool sit_seek(const PersistArgs &a, int grid, int c, SIt &it) {
+  for (; it.step < a.steps; it.step++, it.p = 0) {
+    for (; it.p < a.nphases; it.p++) {
+      const PPhase &ph = a.phases[it.p];
+      if (ph.kind != PH_GEMV) continue;
+      int u0, u1;
+      unit_range(ph.g.tiles, ph.g.nkb, grid, c, u0, u1);
+      if (u0 >= u1) continue;
+      it.u0 = it.s0 = u0;
+      it.u1 = u1;
+      it.k = slot_units(ph.g.type);
+      it.CB = chunk_bytes(ph.g.type);
+      it.w = ph.g.w;
+      return true;
+    }
+  }
+  return false;
+}
+__device__ bool sit_next(const PersistArgs &a, int grid, int c, SIt &it) {
+  it.s0 += it.k;
+  if (it.s0 < it.u1) return true;
+  it.p++;
+  return sit_seek(a, grid, c, it);
+}
+
+
+__device__ __forceinline__ void prefetch_l2(const void *src, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// Producer (lane 0 of warp 9): every weight chunk of this CTA, in execution order,
+// into the ring; optionally the same stream a.l2_ahead stages earlier into L2, so
+// HBM keeps streaming while the other warps wait at barriers.
+__device__ void producer(const PersistArgs &a, const Ring &R, volatile int *stop) {
+  if ((threadIdx.x & 31) != 0) return;
+  const int grid = gridDim.x, c = blockIdx.x;
+  SIt f{0, 0, 0, 0, 0, 0, 0, nullptr};
+  SIt pf = f;
+  bool fv = sit_seek(a, grid, c, f), pv = sit_seek(a, grid, c, pf);
+  int ahead = 0;
+  unsigned g = 0;
+  while (fv) {
+    while (pv && ahead < a.l2_ahead) {
+      prefetch_l2(pf.w + (size_t)pf.s0 * pf.CB, (unsigned)(min(pf.k, pf.u1 - pf.s0) * pf.CB));
+      pv = sit_next(a, grid, c, pf);
+      ahead++;
+    }
+    const int slot = g % R.ns;
+    if (!mbar_wait(R.empty + slot, ((g / R.ns) & 1u) ^ 1u, stop, a.status)) break;
+    const int n = min(f.k, f.u1 - f.s0);
+    if (f.s0 == f.u0) P_TRACE(f.step, f.p, 4);
+    if (f.s0 + f.k >= f.u1) P_TRACE(f.step, f.p, 5);
+    mbar_expect_tx(R.full + slot, (unsigned)(n * f.CB));
+    bulk_g2s(R.slots + (size_t)slot * P_SLOT_BYTES, f.w + (size_t)f.s0 * f.CB, (unsigned)(n * f.CB), R.full + slot);
+    g++;
+    fv = sit_next(a, grid, c, f);
+    ahead--;
+  }
+  // copies issued but not consumed (an early stop) must land before the CTA exits
+  const unsigned first = g > (unsigned)R.ns ? g - R.ns : 0u;
+  for (unsigned q = first; q < g; q++) {
+    const uint64_t t0 = gtime();
+    while (!mbar_test(R.full + q % R.ns, (q / R.ns) & 1u)) {
+      if (gtime() - t0 > P_TIMEOUT_NS) break;
+      __nanosleep(64);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  Ring R;
+  R.ns = a.nstage;
+  R.full = reinterpret_cast<uint64_t *>(smem);
+  R.empty = R.full + P_MAXSTAGES;
+  R.done = R.empty + P_MAXSTAGES;
+  R.resfree = R.done + P_RES_STAGES;
+  R.slots = smem + 256;
+  uint8_t *xs = R.slots + (size_t)R.ns * P_SLOT_BYTES;
+  PShared &sh = *reinterpret_cast<PShared *>(xs + a.xs_bytes);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    for (int i = 0; i < R.ns; i++) {
+      mbar_init(R.full + i, 1);
+      mbar_init(R.empty + i, P_CWARPS);
+    }
+    for (int i = 0; i < P_RES_STAGES; i++) {
+      mbar_init(R.done + i, P_CWARPS);
+      mbar_init(R.resfree + i, 1);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (tid < 4) sh.flags[tid] = 0;
+  __syncthreads();
+  volatile int *stop = &sh.flags[0];
+  if (warp == P_PWARP) {
+    producer(a, R, stop);
+    return;
+  }
+
+  // ---------------- compute warps (0..7) and the epilogue warp (8)
+  const bool comp = warp < P_CWARPS, epi = warp == P_EWARP;
+  const int grid = gridDim.x, c = blockIdx.x;
+  unsigned gen = 0;
+  if (tid == 0) gen = ld_acquire(a.bar + 1);
+  unsigned g = 0;  // ring stage counter, in step with the producer
+  int token = a.first;
+  bool att_staged = false;  // attention stage 0 was filled during the previous phase
+  for (int step = 0; step < a.steps; step++) {
+    const int pos = a.start + step;
+    // embedding row of the token (engine.ts:140-145), spread over the CTAs
+    if (comp) {
+      const int per = (a.hidden + grid - 1) / grid;
+      const int lo = c * per, hi = min(a.hidden, lo + per);
+      for (int e = lo + tid; e < hi; e += P_CWARPS * 32) a.x[e] = p_embed_value(a, token, e) * a.embd_scale;
+    }
+    if (!grid_sync(a, gen, stop)) break;
+    bool alive = true;
+    for (int p = 0; p < a.nphases && alive; p++) {
+      const PPhase &ph = a.phases[p];
+      if (tid == 0) P_TRACE(step, p, 0);
+      if (ph.kind == PH_ATTN) {
+        const PAttn &A = ph.a;
+        int chunk, nsp;
+        attn_split(A, pos, a.nsp_max, chunk, nsp);
+        const int items = A.kv_heads * nsp;
+        if (warp < 4)
+          for (int it = c; it < items; it += grid)
+            p_attn_item(A, pos, it / nsp, it % nsp, nsp, chunk, a.nsp_max, reinterpret_cast<float *>(xs), a.att_part, a.att_ctr,
+                        &sh.flags[1], it == c && att_staged);
+        att_staged = false;
+        if (tid == 0) P_TRACE(step, p, 3);
+        alive = grid_sync(a, gen, stop);
+        continue;
+      }
+      // ---- GEMV phase
+      const PGemv &pg = ph.g;
+      const int nkb = pg.nkb, k = slot_units(pg.type), CB = chunk_bytes(pg.type);
+      int u0, u1;
+      unit_range(pg.tiles, nkb, grid, c, u0, u1);
+      if (comp) {
+        // when attention follows, warps 0..3 start copying this CTA's first K/V tile now
+        // (rows of earlier positions only) into attention stage 0, above the digit records
+        if (p + 1 < a.nphases && a.phases[p + 1].kind == PH_ATTN && warp < 4) {
+          const PAttn &A = a.phases[p + 1].a;
+          if (px_bytes(pg.cols) <= (size_t)attn_stage_floats(A.hd) * 4) {
+            int chunk, nsp;
+            attn_split(A, pos, a.nsp_max, chunk, nsp);
+            if (c < A.kv_heads * nsp) {
+              const int kh = c / nsp, sp = c % nsp;
+              const int end = pos + 1, begin = end - (end < A.window ? end : A.window);
+              const int p0 = begin + sp * chunk, p1 = min(end, p0 + chunk);
+              p_attn_stage(A, pos, kh, p1, p0, reinterpret_cast<float *>(xs), 0, tid);
+              att_staged = true;
+            }
+          }
+        }
+        const bool q6 = pg.type == Q6_K;
+        const PX X = px_carve(xs, pg.cols);
+        p_digitise(pg.x, pg.norm_w, pg.eps, pg.cols, q6, X, sh.red, warp, lane);
+        bar_comp();
+        if (tid == 0) P_TRACE(step, p, 1);
+        const PLane PL = p_lane(lane);
+        // this warp's chunks: u0 + warp, u0 + warp + 8, ... (tile t, super-block kb)
+        int nu = u0 + warp, kb = nkb ? nu % nkb : 0;
+        for (int s0 = u0; s0 < u1; s0 += k, g++) {
+          const int s1 = min(u1, s0 + k), slot = g % R.ns, rs = g % P_RES_STAGES;
+          // this warp's chunks of the stage (at most one: k <= 16 = P_CWARPS), result kept in registers
+          float r[1][2] = {{0.f, 0.f}};
+          int nmine = 0;
+          const int first = nu;
+          if (mbar_wait(R.full + slot, (g / R.ns) & 1u, stop, a.status)) {
+            const uint8_t *base = R.slots + (size_t)slot * P_SLOT_BYTES;
+            for (; nu < s1; nu += P_CWARPS, nmine++) {
+              float acc[2] = {0.f, 0.f};
+              const uint8_t *cp = base + (size_t)(nu - s0) * CB;
+              if (q6) p_q6k(cp, kb, X, PL, lane, acc);
+              else p_q4k(cp, kb, X, PL, lane, acc);
+              acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 1);
+              acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 2);
+              acc[1] += __shfl_xor_sync(0xffffffffu, acc[1], 1);
+              acc[1] += __shfl_xor_sync(0xffffffffu, acc[1], 2);
+              r[0][0] = acc[0];
+              r[0][1] = acc[1];
+              kb += P_CWARPS;
+              while (kb >= nkb) kb -= nkb;
+            }
+          } else {
+            while (nu < s1) nu += P_CWARPS;  // winding down: keep the unit cursor in step
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(R.empty + slot);  // the weight slot may be refilled
+          if (mbar_wait(R.resfree + rs, ((g / P_RES_STAGES) & 1u) ^ 1u, stop, a.status) && (lane & 3) == 0) {
+            for (int i = 0; i < nmine; i++) {
+              sh.res[rs][first + i * P_CWARPS - s0][lane >> 2] = r[i][0];
+              sh.res[rs][first + i * P_CWARPS - s0][(lane >> 2) + 8] = r[i][1];
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(R.done + rs);
+        }
+        if (tid == 0) P_TRACE(step, p, 2);
+#ifdef WGD_PERSIST_TRACE
+        if (tid == 0 && (blockIdx.x == 0 || blockIdx.x == 100) && step < TR_STEPS) {
+          g_trace[blockIdx.x == 0 ? 0 : 1][step][p][6] = g_wait_acc[blockIdx.x == 0 ? 0 : 1];
+          g_wait_acc[blockIdx.x == 0 ? 0 : 1] = 0;
+        }
+#endif
+      } else {
+        // epilogue warp: tile sums in k-block order, then the tile's epilogue
+        GemvCtx C;
+        C.g = &pg;
+        C.best_v = -FLT_MAX;
+        C.best_i = -1;
+        int t = nkb ? u0 / nkb : 0, kbe = 0;
+        float run = 0.f;
+        for (int s0 = u0; s0 < u1; s0 += k, g++) {
+          const int n = min(k, u1 - s0), rs = g % P_RES_STAGES;
+          if (mbar_wait(R.done + rs, (g / P_RES_STAGES) & 1u, stop, a.status)) {
+            float v[P_STAGE_UNITS];
+#pragma unroll
+            for (int j = 0; j < P_STAGE_UNITS; j++) v[j] = (j < n && lane < 16) ? sh.res[rs][j][lane] : 0.f;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(R.resfree + rs);  // results copied out
+#pragma unroll
+            for (int j = 0; j < P_STAGE_UNITS; j++) {
+              if (j < n) {
+                run += v[j];
+                if (++kbe == nkb) {
+                  p_epilogue(C, t, run, lane);
+                  run = 0.f;
+                  kbe = 0;
+                  t++;
+                }
+              }
+            }
+          } else {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(R.resfree + rs);
+          }
+        }
+        if (lane == 0) P_TRACE(step, p, 3);
+        if (pg.argmax) {
+          float bv = C.best_v;
+          int bi = C.best_i;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+          }
+          if (lane == 0) {
+            __stcg(a.cand + c, make_float2(bv, __int_as_float(bi)));
+            if (c == 0 && a.cancel && *(volatile const int *)a.cancel) atomicExch(a.status + 2, 1);
+          }
+        }
+      }
+      alive = grid_sync(a, gen, stop);
+    }
+    if (!alive) break;
+    // greedy token: the best candidate of all CTAs (every CTA computes the same)
+    {
+      float bv = -FLT_MAX;
+      int bi = -1;
+      for (int i = tid; i < grid; i += (P_CWARPS + 1) * 32) {
+        const float2 cv = __ldcg(a.cand + i);
+        const int ci = __float_as_int(cv.y);
+        if (better(cv.x, ci, bv, bi)) { bv = cv.x; bi = ci; }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+      }
+      if (lane == 0) sh.best[warp] = make_float2(bv, __int_as_float(bi));
+      bar_all();
+      if (tid == 0) {
+        float v = -FLT_MAX;
+        int i = -1;
+        for (int w = 0; w <= P_CWARPS; w++) {
+          const float ov = sh.best[w].x;
+          const int oi = __float_as_int(sh.best[w].y);
+          if (better(ov, oi, v, i)) { v = ov; i = oi; }
+        }
+        sh.flags[2] = i;
+      }
+      bar_all();
+      token = sh.flags[2];
+      const bool cancelled = __ldcg(a.status + 2) != 0;
+      if (c == 0 && tid == 0) {
+        a.tokens[step] = token;
+        a.status[1] = step + 1;
+        if (token < 0) atomicCAS(a.status, 0, 2);
+        else if (cancelled && step + 1 < a.steps) atomicCAS(a.status, 0, 3);
+      }
+      if (token < 0 || cancelled) break;
+    }
+  }
+  if (tid == 0) *stop = 1;  // releases a producer still waiting for a free slot
+  (void)epi;
+}
+
+}  // namespace
+
+#ifdef WGD_PERSIST_TRACE
+extern "C" __attribute__((visibility("default"))) int wgd_debug_persist_trace(uint64_t *out, size_t n) {
+  const size_t bytes = sizeof(g_trace) < n * sizeof(uint64_t) ? sizeof(g_trace) : n * sizeof(uint64_t);
+  return (int)cudaMemcpyFromSymbol(out, g_trace, bytes);
+}
+extern "C" __attribute__((visibility("default"))) int wgd_debug_persist_bars(uint64_t *out, int reset) {
+  if (reset) {
+    static int zeros[160] = {0};
+    return (int)cudaMemcpyToSymbol(g_bar_index, zeros, sizeof(zeros));
+  }
+  return (int)cudaMemcpyFromSymbol(out, g_bars, sizeof(g_bars));
+}
+#endif
+
+// ------------------------------------------------------------------ host side
+
+static int attn_smem_bytes(int group, int hd) { return 4 * (group * hd + 2 * hd + 2 * 2 * 32 * (hd + 4)); }
+
+size_t persist_smem_bytes(int max_cols, int group, int hd, int nstage, int *xs) {
+  size_t x = px_bytes(max_cols);
+  const size_t at = (size_t)attn_smem_bytes(group, hd);
+  if (at > x) x = at;
+  x = (x + 127) & ~(size_t)127;
+  if (xs) *xs = (int)x;
+  return 256 + (size_t)nstage * P_SLOT_BYTES + x + sizeof(PShared);
+}
+
+int persist_max_stages(int max_cols, int group, int hd) {
+  const size_t limit = 227 * 1024;
+  const size_t fixed = persist_smem_bytes(max_cols, group, hd, 0, nullptr);
+  if (fixed >= limit) return 0;
+  int ns = (int)((limit - fixed) / P_SLOT_BYTES);
+  return ns > P_MAXSTAGES ? P_MAXSTAGES : ns;
+}
+
+cudaError_t launch_persist(const PersistArgs &a, int grid, cudaStream_t s) {
+  const size_t smem = 256 + (size_t)a.nstage * P_SLOT_BYTES + (size_t)a.xs_bytes + sizeof(PShared);
+  static size_t attr = 0;
+  if (attr < smem) {
+    cudaError_t e = cudaFuncSetAttribute(persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(P_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr1[1];
+  attr1[0].id = cudaLaunchAttributeCooperative;
+  attr1[0].val.cooperative = 1;
+  cfg.attrs = attr1;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, persist_kernel, a);
+}
+
+}  // namespace wgd
