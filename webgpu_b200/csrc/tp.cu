@@ -11,6 +11,7 @@
 // e+2 after every peer has entered e+1, i.e. finished reading e.
 // A wait that runs out sets an error word (read by the host after the forward)
 // and lets the kernel finish; nothing traps.
+#include <algorithm>
 #include <cstring>
 #include "common.cuh"
 #include "tp.h"
@@ -226,7 +227,14 @@ __global__ void argmax_gather_kernel(const TpDev d, int *idx, float *val, int vo
   atomicExch(&hdr(d, d.rank)->epoch, e);
 }
 
-__device__ __forceinline__ int part_lo(int total, int r, int size) { return (int)((long long)total * r / size); }
+
+// First vocabulary row of rank j: the vocabulary is split in whole 16-row tiles (the LM head's
+// tile layout), rank j owning tiles [tiles*j/size, tiles*(j+1)/size).
+__device__ __forceinline__ int vocab_lo(int total, int j, int size) {
+  const int tiles = (total + 15) / 16;
+  const int lo = (int)((long long)tiles * j / size) * 16;
+  return lo < total ? lo : total;
+}
 
 __global__ void gather_rows_kernel(const TpDev d, float *rows, int total, unsigned long long limit) {
   __shared__ unsigned e_s;
@@ -237,7 +245,7 @@ __global__ void gather_rows_kernel(const TpDev d, float *rows, int total, unsign
   const int c = blockIdx.x;
   // push my slice c
   {
-    const int lo = part_lo(total, d.rank, d.size), hi = part_lo(total, d.rank + 1, d.size), cnt = hi - lo;
+    const int lo = vocab_lo(total, d.rank, d.size), hi = vocab_lo(total, d.rank + 1, d.size), cnt = hi - lo;
     const int ch = (cnt + gridDim.x - 1) / gridDim.x, a = lo + c * ch, b = min(hi, a + ch);
     for (int j = 0; j < d.size; j++) {
       float *g = reinterpret_cast<float *>(d.buf[j] + d.gather);
@@ -255,7 +263,7 @@ __global__ void gather_rows_kernel(const TpDev d, float *rows, int total, unsign
   __syncthreads();
   const float *g = reinterpret_cast<const float *>(d.buf[d.rank] + d.gather);
   for (int j = 0; j < d.size; j++) {
-    const int lo = part_lo(total, j, d.size), hi = part_lo(total, j + 1, d.size), cnt = hi - lo;
+    const int lo = vocab_lo(total, j, d.size), hi = vocab_lo(total, j + 1, d.size), cnt = hi - lo;
     const int ch = (cnt + gridDim.x - 1) / gridDim.x, a = lo + c * ch, b = min(hi, a + ch);
     for (int i = a + threadIdx.x; i < b; i += blockDim.x) rows[i] = __ldcg(g + i);
   }
@@ -289,8 +297,11 @@ int tp_argmax_gather(TpComm *t, int *idx, float *val, int vocab0, cudaStream_t s
 
 int tp_gather_rows(TpComm *t, float *rows, int total, int vocab0, int count, cudaStream_t s, unsigned long long spin_limit,
                    std::string *err) {
-  (void)vocab0;
-  (void)count;
+  // the kernel derives every rank's rows from the tile rule; they must agree with the caller's shard
+  const int tiles = (total + 15) / 16;
+  const int lo = std::min(total, (int)((long long)tiles * t->rank / t->size) * 16);
+  const int hi = std::min(total, (int)((long long)tiles * (t->rank + 1) / t->size) * 16);
+  if (lo != vocab0 || hi - lo != count) return err_out(err, "vocabulary shard does not follow the 16-row tile split", 1);
   if (!t->opened) return err_out(err, "tensor-parallel peers are not open (call wgd_tp_open_peers)", 6);
   if ((size_t)total > t->L.gcap) return err_out(err, "gather larger than the exchange area", 1);
   cudaError_t e = launch_k(gather_rows_kernel, dim3(TP_CTAS), dim3(256), 0, s, true, t->dev, rows, total, limit_or_default(spin_limit));
