@@ -1,0 +1,111 @@
+"""Small fixed workloads for profiling the library's kernels on one GPU (run them under
+`ncu`, or alone to print CUDA-event timings):
+
+    python -m webgpu_b200.probe gemv ROWS COLS TYPE [LAUNCHES]   # wgd_op_gemv_tiled on random blocks
+    python -m webgpu_b200.probe attention                        # wgd_op_attention, decode, L = 512/2048/4096
+    python -m webgpu_b200.probe decode LAYERS STEPS [PERSISTENT]  # Llama-3-8B-width model, wgd_decode
+
+`gemv` repacks random GGUF blocks of TYPE (12 = Q4_K, 14 = Q6_K) into the tile layout once and calls the
+tiled GEMV LAUNCHES times (default 5). `attention` keeps 24 K/V caches of [8][4096][128] fp32 (more than
+L2) and times 24 graph-captured launches per length. `decode` loads the synthetic Llama-3-8B
+architecture (seed 2, Q4_K layers, Q6_K head) with LAYERS layers, prefills 512 tokens in batches of 128
+and times `wgd_decode` of STEPS tokens three times (PERSISTENT 1: the persistent kernel, 0: the
+per-kernel path).
+"""
+import ctypes
+import sys
+
+from . import _native, synth
+
+
+def gemv(rows: int, cols: int, ttype: int, launches: int = 5) -> None:
+    import torch
+    L = _native.lib()
+    raw = synth.random_blocks(ttype, rows * cols // synth.BLOCK[ttype][0], 2, 99)
+    nb = L.wgd_tiled_bytes(ttype, rows, cols)
+    rd = torch.from_numpy(raw).cuda()
+    m = torch.empty(nb + 16, dtype=torch.uint8, device="cuda")
+    _native.check(L.wgd_op_repack_tiled(ttype, rows, cols, rd.data_ptr(), m.data_ptr(), None))
+    x = torch.randn(cols, device="cuda")
+    y = torch.empty(rows, device="cuda")
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(launches):
+        _native.check(L.wgd_op_gemv_tiled(ttype, rows, cols, m.data_ptr(), x.data_ptr(), 1, y.data_ptr(), None))
+    e1.record()
+    torch.cuda.synchronize()
+    print(f"gemv type {ttype} {rows}x{cols}: {e0.elapsed_time(e1) / launches * 1000:.2f} us/launch (L2-resident after the first)")
+
+
+def attention(heads: int = 32, kv: int = 8, hd: int = 128, cap: int = 4096, copies: int = 24) -> None:
+    import torch
+    L = _native.lib()
+    ks = [torch.randn(kv, cap, hd, device="cuda") for _ in range(copies)]
+    vs = [torch.randn(kv, cap, hd, device="cuda") for _ in range(copies)]
+    q = torch.randn(heads, hd, device="cuda")
+    out = torch.empty(heads, hd, device="cuda")
+    for start in (511, 2047, 4095):
+        def launch_all(stream):
+            for i in range(copies):
+                _native.check(L.wgd_op_attention(q.data_ptr(), ks[i].data_ptr(), vs[i].data_ptr(), out.data_ptr(), 1, heads, kv,
+                                                 hd, start, 0.088, cap, cap, stream))
+        launch_all(None)
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            launch_all(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / copies * 1000
+        alg = (start + 1) * kv * hd * 4 * 2
+        print(f"attention decode L={start + 1}: {us:7.2f} us  {alg / us / 1e3:7.1f} GB/s", flush=True)
+
+
+def decode(layers: int, steps: int, persistent: int = 1) -> None:
+    from .engine import PagedEngine
+    from .source import MemorySource
+    spec = synth.baseline_spec(3, layers=layers)
+    img = synth.build_gguf(spec)
+    e = PagedEngine()
+    e.load(MemorySource(img), {"contextLength": 4096, "batchSize": 128, "performance": "fast", "gpuBudgetMiB": 100000})
+    L = _native.lib()
+    L.wgd_set_persistent(e.ctx, persistent)
+    prompt = list(synth.uniform_ids(512, 128256, seed=2))
+    tok = None
+    for i in range(0, 512, 128):
+        tok = e.forward(prompt[i:i + 128], i, i + 128 == 512)
+    buf = (ctypes.c_int32 * steps)()
+    _native.check(L.wgd_decode(e.ctx, tok, 512, steps, buf))
+    st = _native.StatsC()
+    for _ in range(3):
+        _native.check(L.wgd_decode(e.ctx, tok, 512, steps, buf))
+        _native.check(L.wgd_stats_get(e.ctx, ctypes.byref(st)))
+        print(f"layers {layers} persistent {persistent}: {st.last_forward_ms / steps * 1000:.1f} us/token ({steps} steps)", flush=True)
+    e.dispose()
+
+
+def main(argv):
+    if not argv:
+        print(__doc__)
+        return 2
+    cmd, args = argv[0], [int(a) for a in argv[1:]]
+    if cmd == "gemv":
+        gemv(*args)
+    elif cmd == "attention":
+        attention(*args)
+    elif cmd == "decode":
+        decode(*args)
+    else:
+        print(__doc__)
+        return 2
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main(sys.argv[1:]))
