@@ -112,15 +112,20 @@ WGD_API int wgd_model_begin(wgd_ctx *ctx, const wgd_model_config *cfg, int conte
 WGD_API int wgd_tensor_register(wgd_ctx *ctx, const char *name, int ggml_type, const uint64_t *dims, int nd,
                         uint64_t file_offset, uint64_t bytes, uint64_t row_bytes);
 WGD_API int wgd_model_end(wgd_ctx *ctx);
-/* Uploads bytes [byte_off, byte_off+n) of a tensor's GGUF data (whole rows) for
- * resident weights; replaces WeightPager.page + Compute.write (pager.ts:25-44). */
+/* Uploads bytes [byte_off, byte_off+n) of a tensor's GGUF data (whole rows); replaces
+ * WeightPager.page + Compute.write (pager.ts:25-44). model_end decides where each matrix lives:
+ * on the device while the budget allows (less a 16 MiB margin), otherwise in pinned host memory
+ * owned by the library, from which every forward streams it page by page (page_bytes, two device
+ * slots, a copy stream); the data is repacked into the device layout either way. */
 WGD_API int wgd_tensor_upload(wgd_ctx *ctx, const char *name, uint64_t byte_off, const void *host, uint64_t n);
-/* Registers a host copy of a tensor's GGUF bytes (kept alive by the caller)
- * from which non-resident pages are streamed; `pinned` != 0 if the memory is
- * page-locked or should be registered as such. */
+/* Uploads a whole tensor from `host` (all of its GGUF bytes; the memory is read during the call
+ * only). `pinned` is a hint that the memory is page-locked. */
 WGD_API int wgd_tensor_host(wgd_ctx *ctx, const char *name, const void *host, int pinned);
-/* Fallback source for streamed pages (ByteSource.read). */
+/* Sets the byte-range reader wgd_load_weights pulls the model through (ByteSource.read,
+ * source.ts:2-6): reads of at most page_bytes (whole rows) into a library-owned buffer. */
 WGD_API int wgd_set_page_reader(wgd_ctx *ctx, wgd_read_fn fn, void *user);
+/* Uploads every tensor this rank needs through the page reader (after model_end). */
+WGD_API int wgd_load_weights(wgd_ctx *ctx);
 /* 1 if every weight needed by forward is resident or has a stream source. */
 WGD_API int wgd_model_ready(wgd_ctx *ctx, int *ready);
 /* Resident weight bytes and streamed weight bytes of the placement plan. */

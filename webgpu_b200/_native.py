@@ -57,6 +57,7 @@ SIGNATURES = {
     "wgd_tensor_upload": (c_int, [c_void_p, c_char_p, c_uint64, c_void_p, c_uint64]),
     "wgd_tensor_host": (c_int, [c_void_p, c_char_p, c_void_p, c_int]),
     "wgd_set_page_reader": (c_int, [c_void_p, READ_FN, c_void_p]),
+    "wgd_load_weights": (c_int, [c_void_p]),
     "wgd_model_ready": (c_int, [c_void_p, ctypes.POINTER(c_int)]),
     "wgd_model_placement": (c_int, [c_void_p, ctypes.POINTER(c_uint64), ctypes.POINTER(c_uint64)]),
     "wgd_forward": (c_int, [c_void_p, ctypes.POINTER(c_int32), c_int, c_int, c_int, ctypes.POINTER(c_int32), ctypes.POINTER(c_float)]),

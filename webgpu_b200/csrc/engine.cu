@@ -14,6 +14,7 @@
 // Single-token forwards are captured once into a CUDA graph (positions live in
 // device memory, so one graph serves every step) and replayed.
 #include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -50,10 +51,14 @@ namespace {
 
 struct DevLinear {
   int type = -1, rows = 0, cols = 0, nb = 0;
-  int64_t drow = 0;    // row layout: bytes per row
-  bool tiled = false;  // tile-16 layout (tensor-core GEMV)
-  uint8_t *w = nullptr;
+  int64_t drow = 0;       // row layout: bytes per row
+  bool tiled = false;     // tile-16 layout (tensor-core GEMV)
+  bool streamed = false;  // kept in pinned host memory and paged through device slots per forward
+  int unit_rows = 1;      // page granularity in rows (a tile, or a gate|up interleave block)
+  uint8_t *w = nullptr;   // device pointer (a mapped host pointer when streamed)
+  const char *label = "";
   int64_t bytes() const { return tiled ? tiled_bytes(type, rows, cols) : drow * rows; }
+  int64_t unit_bytes() const { return tiled ? (int64_t)(cols / 256) * tile_chunk_bytes(type) : drow * unit_rows; }
 };
 
 enum Role {
@@ -151,6 +156,20 @@ struct wgd_ctx {
   std::string persist_why = "not built";
   PersistArgs pargs{};
   int *h_status = nullptr;  // pinned mirror of pargs.status
+  // weight pager (WeightPager, pager.ts): matrices that do not fit the budget live in pinned host
+  // memory and stream through two device page slots on a copy stream
+  std::vector<DevLinear *> pending;  // matrices placed by model_end, in execution order
+  std::vector<void *> host_allocs;
+  bool paging = false;
+  uint8_t *slot[2] = {nullptr, nullptr};
+  size_t slot_bytes = 0;
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t copied[2] = {nullptr, nullptr}, freed[2] = {nullptr, nullptr};
+  unsigned page_seq = 0;
+  wgd_read_fn reader = nullptr;  // ByteSource.read for wgd_load_weights
+  void *reader_user = nullptr;
+  uint8_t *reader_buf = nullptr;
+  uint64_t reader_buf_bytes = 0;
 };
 // h_io slots: [0] start, [1] argmax, [2..1015] ids, [1016..1019] persistent status, [1020] cancel word
 constexpr int IO_STATUS = 1016, IO_CANCEL = 1020;
@@ -189,6 +208,9 @@ static void free_all(wgd_ctx *ctx) {
   for (auto &a : ctx->allocs) cudaFree(a.p);
   ctx->allocs.clear();
   ctx->allocated = 0;
+  for (void *h : ctx->host_allocs) cudaFreeHost(h);
+  ctx->host_allocs.clear();
+  ctx->pending.clear();
 }
 
 static bool parse_layer_name(const std::string &name, int &layer, Role &role) {
@@ -263,11 +285,21 @@ void wgd_destroy(wgd_ctx *ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->copy_stream) cudaStreamSynchronize(ctx->copy_stream);
   if (ctx->tp) tp_destroy(ctx->tp);
   free_all(ctx);
   if (ctx->h_io) cudaFreeHost(ctx->h_io);
+  if (ctx->reader_buf) cudaFreeHost(ctx->reader_buf);
   if (ctx->ev0) cudaEventDestroy(ctx->ev0);
   if (ctx->ev1) cudaEventDestroy(ctx->ev1);
+  for (int i = 0; i < 2; i++) {
+    if (ctx->copied[i]) cudaEventDestroy(ctx->copied[i]);
+    if (ctx->freed[i]) cudaEventDestroy(ctx->freed[i]);
+  }
+  if (ctx->copy_stream) {
+    cudaStreamSynchronize(ctx->copy_stream);
+    cudaStreamDestroy(ctx->copy_stream);
+  }
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
 }
@@ -365,7 +397,55 @@ static int alloc_linear(wgd_ctx *ctx, DevLinear &L, int type, int rows, int cols
     if (pf > ctx->g2_part_floats) ctx->g2_part_floats = pf;
     if ((rows + 15) / 16 > ctx->g2_ctr_count) ctx->g2_ctr_count = (rows + 15) / 16;
   }
-  return ctx_alloc_t(ctx, &L.w, (size_t)L.bytes() + 16, label);
+  L.unit_rows = L.tiled ? TILE_ROWS : GEMV_ROWS;  // pages cut at whole tiles / whole gate|up interleave blocks
+  L.label = label;
+  ctx->pending.push_back(&L);  // storage is placed once every fixed buffer is (place_matrices)
+  return WGD_OK;
+}
+
+// Places the matrices in execution order: on the device while they fit the budget (less a 16 MiB
+// margin, the cacheBudget rule of pager.ts:22), the rest in pinned host memory mapped into the
+// device address space (repacked there at upload, copied page by page into the slots per forward).
+static int place_matrices(wgd_ctx *ctx) {
+  uint64_t need = 0;
+  int64_t unit_max = 0;
+  for (DevLinear *L : ctx->pending) {
+    need += (uint64_t)align_up(L->bytes() + 16, 256);
+    unit_max = std::max(unit_max, L->unit_bytes());
+  }
+  const uint64_t margin = 16u << 20;
+  ctx->paging = ctx->allocated + need > ctx->budget;
+  int rc;
+  if (ctx->paging) {
+    ctx->slot_bytes = std::max<size_t>(ctx->page_bytes, (size_t)unit_max);
+    for (int i = 0; i < 2; i++)
+      if ((rc = ctx_alloc_t(ctx, &ctx->slot[i], ctx->slot_bytes, "page slot"))) return rc;
+    CK(cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking));
+    for (int i = 0; i < 2; i++) {
+      CK(cudaEventCreateWithFlags(&ctx->copied[i], cudaEventDisableTiming));
+      CK(cudaEventCreateWithFlags(&ctx->freed[i], cudaEventDisableTiming));
+      CK(cudaEventRecord(ctx->freed[i], ctx->stream));
+    }
+    ctx->st.page_bytes = ctx->slot_bytes;
+  }
+  uint64_t resident = 0;
+  for (DevLinear *L : ctx->pending) {
+    const uint64_t size = (uint64_t)align_up(L->bytes() + 16, 256);
+    if (!ctx->paging || ctx->allocated + size + margin <= ctx->budget) {
+      if ((rc = ctx_alloc_t(ctx, &L->w, (size_t)size, L->label))) return rc;
+      resident += size;
+    } else {
+      void *h = nullptr;
+      cudaError_t e = cudaHostAlloc(&h, size, cudaHostAllocMapped | cudaHostAllocPortable);
+      if (e != cudaSuccess) return fail(WGD_ECUDA, std::string("pinned host memory for a streamed matrix: ") + cudaGetErrorString(e));
+      ctx->host_allocs.push_back(h);
+      memset(h, 0, size);
+      CK(cudaHostGetDevicePointer((void **)&L->w, h, 0));
+      L->streamed = true;
+    }
+  }
+  ctx->st.cache_bytes = resident;
+  return WGD_OK;
 }
 
 // A matrix part: GGUF rows [src_begin, src_end) -> device rows (map), columns [blk0, blk0+nbl) in blocks.
@@ -394,6 +474,7 @@ static int build_persist_plan(wgd_ctx *ctx) {
   ctx->persist_ok = false;
   auto no = [&](const char *why) { ctx->persist_why = why; return WGD_OK; };
   if (ctx->tp_size != 1) return no("tensor-parallel runs use the per-kernel path");
+  if (ctx->paging) return no("weights are paged through device slots (per-kernel path)");
   if (c.family == 1) return no("the gemma block (post-norms) uses the per-kernel path");
   const int G = ctx->kv_l ? ctx->heads_l / ctx->kv_l : 0;
   if (hd % 4 || hd > 256 || G < 1 || G > 8) return no("attention shape outside the persistent kernel");
@@ -680,17 +761,13 @@ extern "C" int wgd_model_end(wgd_ctx *ctx) {
   }
 
   // ---- embedding (replicated: any id can appear) and LM head (vocab rows of this rank)
-  if ((rc = alloc_linear(ctx, ctx->embd, embd->type, c.vocab, H, "token_embd"))) return rc;
-  place(embd, &ctx->embd, 0, c.vocab, 0, 0, 0, ctx->embd.nb);
-  if (ctx->tied) {
-    ctx->lm = ctx->embd;
-    ctx->lm.w = ctx->embd.w + (ctx->embd.tiled ? (int64_t)(ctx->vocab0 / 16) * ctx->embd.nb * tile_chunk_bytes(embd->type)
-                                               : (int64_t)ctx->vocab0 * ctx->embd.drow);
-    ctx->lm.rows = ctx->vocab_l;
-  } else {
+  // the head is used every token, the embedding table one row per token: place the head first
+  if (!ctx->tied) {
     if ((rc = alloc_linear(ctx, ctx->lm, output->type, ctx->vocab_l, H, "output"))) return rc;
     place(output, &ctx->lm, ctx->vocab0, ctx->vocab0 + ctx->vocab_l, 0, 0, 0, ctx->lm.nb);
   }
+  if ((rc = alloc_linear(ctx, ctx->embd, embd->type, c.vocab, H, "token_embd"))) return rc;
+  place(embd, &ctx->embd, 0, c.vocab, 0, 0, 0, ctx->embd.nb);
   if ((rc = ctx_alloc_t(ctx, &ctx->out_norm, H, "output_norm"))) return rc;
   place_vec(ctx, onorm, ctx->out_norm, 0, H);
 
@@ -743,6 +820,13 @@ extern "C" int wgd_model_end(wgd_ctx *ctx) {
     return rc;
   if (tp > 1) {
     if ((rc = tp_create(&ctx->tp, ctx->tp_rank, tp, (size_t)B * H, &g_err))) return rc;
+  }
+  if ((rc = place_matrices(ctx))) return rc;
+  if (ctx->tied) {  // the head is this rank's vocabulary rows of the embedding table
+    ctx->lm = ctx->embd;
+    ctx->lm.w = ctx->embd.w + (ctx->embd.tiled ? (int64_t)(ctx->vocab0 / 16) * ctx->embd.nb * tile_chunk_bytes(embd->type)
+                                               : (int64_t)ctx->vocab0 * ctx->embd.drow);
+    ctx->lm.rows = ctx->vocab_l;
   }
   if ((rc = build_persist_plan(ctx))) return rc;
   ctx->ended = true;
@@ -810,14 +894,48 @@ extern "C" int wgd_tensor_host(wgd_ctx *ctx, const char *name, const void *host,
   if (!ctx || !name || !host) return fail(WGD_EINVAL, "null argument");
   TensorRec *t = find(ctx, name);
   if (!t) return fail(WGD_EINVAL, std::string("unknown tensor ") + name);
-  t->host = host;
-  (void)pinned;
-  return WGD_OK;
+  (void)pinned;  // the staging copy below reads pageable and page-locked memory alike
+  return wgd_tensor_upload(ctx, name, 0, host, t->bytes);
 }
 
 extern "C" int wgd_set_page_reader(wgd_ctx *ctx, wgd_read_fn fn, void *user) {
   if (!ctx) return fail(WGD_EINVAL, "null context");
-  (void)fn; (void)user;
+  ctx->reader = fn;
+  ctx->reader_user = user;
+  return WGD_OK;
+}
+
+extern "C" int wgd_load_weights(wgd_ctx *ctx) {
+  if (!ctx) return fail(WGD_EINVAL, "null context");
+  if (!ctx->ended) return fail(WGD_ESTATE, "load_weights requires model_end first");
+  if (!ctx->reader) return fail(WGD_ESTATE, "no page reader set (wgd_set_page_reader)");
+  const uint64_t page = std::max<uint64_t>(ctx->page_bytes, 1u << 20);
+  if (!ctx->reader_buf || ctx->reader_buf_bytes < page) {
+    if (ctx->reader_buf) cudaFreeHost(ctx->reader_buf);
+    ctx->reader_buf = nullptr;
+    CK(cudaMallocHost((void **)&ctx->reader_buf, page));
+    ctx->reader_buf_bytes = page;
+  }
+  for (auto &t : ctx->tensors) {
+    if (!t.needed || (t.vec ? t.uploaded_rows >= 1 : t.uploaded_rows >= t.rows)) continue;
+    // whole rows per read; a vector (or a row wider than a page) is read whole
+    const uint64_t step = t.vec || t.row_bytes > page ? t.bytes : page / t.row_bytes * t.row_bytes;
+    if (step > ctx->reader_buf_bytes) {
+      cudaFreeHost(ctx->reader_buf);
+      ctx->reader_buf = nullptr;
+      CK(cudaMallocHost((void **)&ctx->reader_buf, step));
+      ctx->reader_buf_bytes = step;
+    }
+    for (uint64_t off = 0; off < t.bytes; off += step) {
+      const uint64_t n = std::min(step, t.bytes - off);
+      const auto r0 = std::chrono::steady_clock::now();
+      if (ctx->reader(ctx->reader_user, t.offset + off, n, ctx->reader_buf) != 0)
+        return fail(WGD_EIO, "page reader failed for " + t.name);
+      ctx->st.read_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - r0).count();
+      int rc;
+      if ((rc = wgd_tensor_upload(ctx, t.name.c_str(), off, ctx->reader_buf, n))) return rc;
+    }
+  }
   return WGD_OK;
 }
 
@@ -849,7 +967,42 @@ extern "C" int wgd_model_placement(wgd_ctx *ctx, uint64_t *resident, uint64_t *s
 // ------------------------------------------------------------------ forward
 
 static int gemv(wgd_ctx *ctx, const DevLinear &L, const float *x, int ldx, const float *norm_w, float *y, int ldy,
+                const float *bias, int epi, int batch);
+
+// A streamed matrix, one page at a time: the copy stream fills slot i (after the GEMV that last
+// read it finished: event freed[i]) from pinned host memory, the compute stream waits for the copy
+// (copied[i]) and runs the GEMV on that page's rows (WeightPager.page, pager.ts:25-44; the copy of
+// the next page overlaps the GEMV of this one).
+static int gemv_paged(wgd_ctx *ctx, const DevLinear &L, const float *x, int ldx, const float *norm_w, float *y, int ldy,
+                      const float *bias, int epi, int batch) {
+  const bool glu = epi == EPI_GLU_SILU || epi == EPI_GLU_GELU;
+  const int64_t ub = L.unit_bytes();
+  const int units = (L.rows + L.unit_rows - 1) / L.unit_rows;
+  const int per_page = (int)std::max<int64_t>(1, (int64_t)ctx->slot_bytes / ub);
+  const uint8_t *host = L.w;  // mapped host pointer: the same address from the host
+  for (int u0 = 0; u0 < units; u0 += per_page) {
+    const int n = std::min(per_page, units - u0);
+    const int r0 = u0 * L.unit_rows, rows = std::min(n * L.unit_rows, L.rows - r0);
+    const int i = (int)(ctx->page_seq++ & 1u);
+    CK(cudaStreamWaitEvent(ctx->copy_stream, ctx->freed[i], 0));
+    CK(cudaMemcpyAsync(ctx->slot[i], host + (int64_t)u0 * ub, (size_t)n * ub, cudaMemcpyHostToDevice, ctx->copy_stream));
+    CK(cudaEventRecord(ctx->copied[i], ctx->copy_stream));
+    CK(cudaStreamWaitEvent(ctx->stream, ctx->copied[i], 0));
+    DevLinear P = L;
+    P.streamed = false;
+    P.w = ctx->slot[i];
+    P.rows = rows;
+    int rc;
+    if ((rc = gemv(ctx, P, x, ldx, norm_w, y + (glu ? r0 / 2 : r0), ldy, bias ? bias + r0 : nullptr, epi, batch))) return rc;
+    CK(cudaEventRecord(ctx->freed[i], ctx->stream));
+    ctx->st.streamed_bytes += (uint64_t)n * ub;
+  }
+  return WGD_OK;
+}
+
+static int gemv(wgd_ctx *ctx, const DevLinear &L, const float *x, int ldx, const float *norm_w, float *y, int ldy,
                 const float *bias, int epi, int batch) {
+  if (L.streamed) return gemv_paged(ctx, L, x, ldx, norm_w, y, ldy, bias, epi, batch);
   const int chunk = L.tiled ? gemv2_max_batch(L.cols) : gemv_max_batch(L.cols);
   ctx->kernels += chunk > 0 ? (batch + chunk - 1) / chunk : 1;
   if (L.tiled) {
@@ -1021,6 +1174,7 @@ extern "C" int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, i
     if (ids[i] < 0 || ids[i] >= ctx->c.vocab) return fail(WGD_EINVAL, "token id out of range");
   if (ctx->cancel.exchange(0)) return fail(WGD_ECANCELLED, "Stopped by user");
   CK(cudaSetDevice(ctx->device));
+  ctx->st.streamed_bytes = 0;
   ctx->h_io[0] = start;
   memcpy(ctx->h_io + 2, ids, sizeof(int32_t) * n);
   CK(cudaEventRecord(ctx->ev0, ctx->stream));
@@ -1031,7 +1185,7 @@ extern "C" int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, i
     ctx->h_io[IO_CANCEL] = 0;
     if ((rc = enqueue_persist(ctx, ids[0], start, 1))) return rc;
     CK(cudaMemcpyAsync(ctx->h_io + 1, ctx->d_tokens, sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream));
-  } else if (n == 1 && ctx->graphs && !gather_logits) {
+  } else if (n == 1 && ctx->graphs && !gather_logits && !ctx->paging) {
     if (!ctx->decode_exec) {
       CK(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
       rc = enqueue_forward(ctx, 1, false);
@@ -1094,7 +1248,8 @@ extern "C" int wgd_decode(wgd_ctx *ctx, int32_t first, int start, int steps, int
     ctx->st.tokens += done;
     return persist_status(ctx);
   }
-  if (!ctx->chain_exec) {
+  ctx->st.streamed_bytes = 0;
+  if (!ctx->chain_exec && !ctx->paging) {
     CK(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
     rc = enqueue_forward(ctx, 1, false, false);
     if (!rc) {
@@ -1110,8 +1265,10 @@ extern "C" int wgd_decode(wgd_ctx *ctx, int32_t first, int start, int steps, int
     CK(cudaGraphInstantiate(&ctx->chain_exec, g, 0));
     ctx->chain_kernels = ctx->kernels;
   }
-  ctx->kernels = ctx->chain_kernels;
-  ctx->st.kernel_launches += (uint64_t)ctx->kernels * steps;
+  if (!ctx->paging) {
+    ctx->kernels = ctx->chain_kernels;
+    ctx->st.kernel_launches += (uint64_t)ctx->kernels * steps;
+  }
   ctx->h_io[0] = start;
   ctx->h_io[2] = first;
   ctx->h_io[3] = 0;
@@ -1120,7 +1277,15 @@ extern "C" int wgd_decode(wgd_ctx *ctx, int32_t first, int start, int steps, int
   CK(cudaMemcpyAsync(ctx->d_step, ctx->h_io + 3, sizeof(int32_t), cudaMemcpyHostToDevice, ctx->stream));
   CK(cudaMemsetAsync(ctx->d_err, 0, sizeof(int32_t), ctx->stream));
   CK(cudaEventRecord(ctx->ev0, ctx->stream));
-  for (int i = 0; i < steps; i++) CK(cudaGraphLaunch(ctx->chain_exec, ctx->stream));
+  if (ctx->paging) {  // paged weights: the same step enqueued per token (copy-stream events do not go in a graph)
+    for (int i = 0; i < steps; i++) {
+      if ((rc = enqueue_forward(ctx, 1, false, false))) return rc;
+      CK(launch_advance(ctx->d_ids, ctx->d_start, ctx->d_argmax, ctx->d_tokens, ctx->d_step, ctx->d_err, ctx->stream, true));
+      ctx->st.kernel_launches += (uint64_t)ctx->kernels + 1;
+    }
+  } else {
+    for (int i = 0; i < steps; i++) CK(cudaGraphLaunch(ctx->chain_exec, ctx->stream));
+  }
   CK(cudaEventRecord(ctx->ev1, ctx->stream));
   CK(cudaMemcpyAsync(tokens_out, ctx->d_tokens, sizeof(int32_t) * steps, cudaMemcpyDeviceToHost, ctx->stream));
   int32_t err = 0;

@@ -216,7 +216,10 @@ class PagedEngine:
             _native.check(L.wgd_model_end(self.ctx), "model_end")
             if self.tp > 1:
                 self._open_peers(o.get("exchange"))
-            self._upload(signal)
+            if o.get("pull"):
+                self._pull()
+            else:
+                self._upload(signal)
             ready = ctypes.c_int(0)
             _native.check(L.wgd_model_ready(self.ctx, ctypes.byref(ready)), "model_ready")
             if not ready.value:
@@ -241,6 +244,24 @@ class PagedEngine:
             raise RuntimeError("handle exchange returned the wrong number of ranks")
         allh = b"".join(handles)
         _native.check(L.wgd_tp_open_peers(self.ctx, ctypes.c_char_p(allh)), "tp_open_peers")
+
+    def _pull(self):
+        """Loads through the library's page reader: the library asks for byte ranges of the model
+        (ByteSource.read, source.ts:2-6) in pages of whole rows."""
+        L = _native.lib()
+        src = self.source
+
+        def read(_user, offset, length, dst):
+            try:
+                data = src.read(offset, length)
+                ctypes.memmove(dst, bytes(data) if not isinstance(data, (bytes, bytearray)) else data, length)
+                return 0
+            except Exception:  # reported by the library as an I/O error
+                return 1
+
+        self._reader = _native.READ_FN(read)  # kept alive while the context exists
+        _native.check(L.wgd_set_page_reader(self.ctx, self._reader, None), "set_page_reader")
+        _native.check(L.wgd_load_weights(self.ctx), "load_weights")
 
     def _upload(self, signal=None):
         L = _native.lib()
