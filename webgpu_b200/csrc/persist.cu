@@ -52,6 +52,17 @@ __device__ __forceinline__ bool mbar_test(uint64_t *b, unsigned parity) {
       : "memory");
   return ok != 0;
 }
+// Blocking form: the hardware suspends the thread until the phase completes or a
+// hardware time limit passes (then false).
+__device__ __forceinline__ bool mbar_try(uint64_t *b, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // bulk copy global -> this CTA's shared memory, completing on mbarrier `bar`
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(su32(dst)),
@@ -109,11 +120,13 @@ __device__ uint64_t g_wait_acc[2];  // ns thread 0 of CTAs 0 / 100 spent waiting
 // (sums each tile's chunk results in k-block order, stores, greedy tracking), 9 producer.
 constexpr int P_EWARP = P_CWARPS, P_PWARP = P_CWARPS + 1;
 constexpr int P_MAXSTAGES = 8, P_STAGE_UNITS = 16, P_RES_STAGES = 8;
+static_assert(P_SLOT_BYTES / 2304 <= P_CWARPS && P_SLOT_BYTES / 2304 <= P_STAGE_UNITS, "a stage holds at most one chunk per compute warp");
 
 // Shared state of one CTA besides the ring and the xs region.
 struct PShared {
   float res[P_RES_STAGES][P_STAGE_UNITS][16];  // per stage (mod P_RES_STAGES): the 16 row sums of each chunk
   float red[P_CWARPS];
+  int dsum[P_CWARPS][48];  // digitiser scratch: one super-block's digit sums per warp
   float2 best[P_CWARPS + 1];
   int flags[4];  // [0] stop (finished / winding down), [1] attention last-arriver, [2] token, [3] stop snapshot
 };
@@ -145,28 +158,30 @@ __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
 // super-block sb,
 //   brec sb*960 + (dg*4 + tig)*80 + j*8 + hi*4   digit plane dg at k = 4tig.. (hi 0) /
 //                                                16+4tig.. (hi 1) of 32-block j
-//   ds   Q4_K: sb*320 + tig*80 + j*8 + pos*4     digit sum over 32-block j of MMA column 2tig+pos
-//        Q6_K: sb*576 + tig*144 + r*8 + pos*4    the same over 16-run r
+//   dsw  sb*256 + lane*8                         the lane's B fragment words (low bytes, high
+//                                                bytes) of the digit sums of MMA column grp = dg:
+//                                                Q4_K: 32-block sums j = 4tig..4tig+3 (tig < 2);
+//                                                Q6_K: 16-run sums r = 4tig..4tig+3; zero elsewhere
 //   sxs[sb]                                      digit scale
 // (records 80 bytes apart: 12 live records fall on 8 bank groups, two wavefronts).
 struct PX {
-  uint8_t *brec, *ds;
+  uint8_t *brec, *dsw;
   float *sxs;
 };
 __host__ __device__ inline size_t px_bytes(int cols) {
   const size_t nsb = (size_t)cols / 256;
-  return nsb * 960 + nsb * 576 + nsb * 4 + 64;
+  return nsb * 960 + nsb * 256 + nsb * 4 + 64;
 }
 __device__ __forceinline__ PX px_carve(uint8_t *xs, int cols) {
   const int nsb = cols >> 8;
   PX X;
   X.brec = xs;
-  X.ds = xs + (size_t)nsb * 960;
-  X.sxs = reinterpret_cast<float *>(X.ds + (size_t)nsb * 576);
+  X.dsw = xs + (size_t)nsb * 960;
+  X.sxs = reinterpret_cast<float *>(X.dsw + (size_t)nsb * 256);
   return X;
 }
-constexpr int P_MAXSBW = 4;  // super-blocks per compute warp: inputs up to 16*4*256 = 16384 wide
-static_assert(P_CWARPS == 16, "digit records assume 16 compute warps");
+constexpr int P_MAXSBW = 5;  // super-blocks per compute warp: inputs up to 14*5*256 = 17920 wide
+static_assert(P_CWARPS * P_MAXSBW * 256 >= 16384, "digit records must cover 16384-wide inputs");
 
 // Lane constants: the lane's B record (dead MMA columns 3..7 reuse plane 0 and get weight 0)
 // and the digit weights of its two D columns n0 = 2tig, n1 = 2tig + 1.
@@ -189,8 +204,8 @@ __device__ __forceinline__ PLane p_lane(int lane) {
 // loads: warp w holds super-blocks w, w+16, ... in registers, the norm's sum of
 // squares comes from the same registers. x ~= s * (a + b/254 + c/254^2), s =
 // max|x|/127 per super-block (the same digits as the stand-alone GEMV).
-__device__ void p_digitise(const float *x, const float *nw, float eps, int cols, bool q6, const PX &X, float *red, int warp,
-                           int lane) {
+__device__ void p_digitise(const float *x, const float *nw, float eps, int cols, bool q6, const PX &X, float *red, int *sums,
+                           int warp, int lane) {
   const int nsb = cols >> 8;
   const int q8 = lane & 7, tg = q8 & 3, hi = q8 >> 2;
   float4 v[P_MAXSBW][2];
@@ -265,27 +280,70 @@ __device__ void p_digitise(const float *x, const float *nw, float eps, int cols,
         s16 += __shfl_xor_sync(0xffffffffu, s16, 1);
         s16 += __shfl_xor_sync(0xffffffffu, s16, 2);   // 16-run 2j + hi
         const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 4);  // 32-block j
-        const int tgn = dg >> 1, pos = dg & 1;          // MMA column dg sits at tig dg/2, component dg%2
         if (q6) {
-          if ((q8 & 3) == 0) *reinterpret_cast<int *>(X.ds + (size_t)sb * 576 + tgn * 144 + (2 * j + hi) * 8 + pos * 4) = s16;
+          if ((q8 & 3) == 0) sums[dg * 16 + 2 * j + hi] = s16;
         } else if (q8 == 0) {
-          *reinterpret_cast<int *>(X.ds + (size_t)sb * 320 + tgn * 80 + j * 8 + pos * 4) = s32;
+          sums[dg * 16 + j] = s32;
         }
       }
     }
+    __syncwarp();
+    // lane (grp = dg, tig) of the digit-sum MMA holds the sums k = 4tig..4tig+3 of column dg,
+    // split into low bytes (unsigned) and high bytes (signed): sum = 256*hi + lo
+    {
+      const int grp = lane >> 2, tig = lane & 3;
+      uint32_t lo = 0u, hw = 0u;
+      if (grp < 3 && (q6 || tig < 2)) {
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+          const int sv = sums[grp * 16 + 4 * tig + m];
+          lo |= ((uint32_t)sv & 255u) << (8 * m);
+          hw |= ((uint32_t)(sv >> 8) & 255u) << (8 * m);
+        }
+      }
+      *reinterpret_cast<uint2 *>(X.dsw + (size_t)sb * 256 + lane * 8) = make_uint2(lo, hw);
+    }
+    __syncwarp();
   }
 }
 
+// MMA shapes with the operand signedness the chunk math needs (D = A*B, zero C).
+__device__ __forceinline__ void mma_k32_uu(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(0u), "r"(0u), "r"(b0), "r"(0u), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+__device__ __forceinline__ void mma_k32_us(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(0u), "r"(0u), "r"(b0), "r"(0u), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+__device__ __forceinline__ void mma_k16_su(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+__device__ __forceinline__ void mma_k16_ss(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
 // One Q4_K tile chunk (16 rows x 256 columns, staged in shared memory at c) against the
-// digit records of super-block kb: the integer formulation of gemv2_impl.cuh.
+// digit records of super-block kb:
+//   sum_j (d*sc_j*q - dmin*mn_j) x = s*(d*sum_j sc_j*D_j - dmin*sum_j mn_j*Sdig_j)
+// The high nibbles enter the MMA as 16*q (byte & 0xF0, still a u8 operand) and are summed
+// separately, then divided by 16 exactly. sum_j mn_j*Sdig_j is itself one small MMA: the six
+// packed 6-bit mins of each row are the A fragment (k = j), the digit sums (split into a low and
+// a high byte) the B fragment.
 __device__ __forceinline__ void p_q4k(const uint8_t *c, int kb, const PX &X, const PLane &P, int lane, float (&acc)[2]) {
   Q4KRegs r;
 #pragma unroll
   for (int g = 0; g < 4; g++) r.qs[g] = *reinterpret_cast<const uint4 *>(c + 512 * g + 16 * lane);
-  const int grp = lane >> 2;
+  const int grp = lane >> 2, tig = lane & 3;
   r.h0 = *reinterpret_cast<const uint4 *>(c + 2048 + 16 * grp);
   r.h1 = *reinterpret_cast<const uint4 *>(c + 2048 + 16 * (grp + 8));
-  const uint32_t M4 = 0x0F0F0F0Fu;
+  const uint32_t M4 = 0x0F0F0F0Fu, H4 = 0xF0F0F0F0u;
   const uint32_t sc_lo0 = r.h0.y & 0x3F3F3F3Fu, mn_lo0 = r.h0.z & 0x3F3F3F3Fu;
   const uint32_t sc_hi0 = (r.h0.w & M4) | ((r.h0.y >> 2) & 0x30303030u);
   const uint32_t mn_hi0 = ((r.h0.w >> 4) & M4) | ((r.h0.z >> 2) & 0x30303030u);
@@ -293,51 +351,59 @@ __device__ __forceinline__ void p_q4k(const uint8_t *c, int kb, const PX &X, con
   const uint32_t sc_hi1 = (r.h1.w & M4) | ((r.h1.y >> 2) & 0x30303030u);
   const uint32_t mn_hi1 = ((r.h1.w >> 4) & M4) | ((r.h1.z >> 2) & 0x30303030u);
   const uint4 *bp = reinterpret_cast<const uint4 *>(X.brec + (size_t)kb * 960 + P.boff);
-  const int4 *dp = reinterpret_cast<const int4 *>(X.ds + (size_t)kb * 320 + P.tig * 80);
   uint4 B[4];
-  int4 DS[4];
 #pragma unroll
-  for (int i = 0; i < 4; i++) { B[i] = bp[i]; DS[i] = dp[i]; }
-  int I00 = 0, I01 = 0, I10 = 0, I11 = 0, M00 = 0, M01 = 0, M10 = 0, M11 = 0;
+  for (int i = 0; i < 4; i++) B[i] = bp[i];
+  const uint2 dw = *reinterpret_cast<const uint2 *>(X.dsw + (size_t)kb * 256 + lane * 8);
+  // mins term: A = mins of rows grp / grp+8 at k = j (tig 0: j 0..3, tig 1: j 4..7)
+  const uint32_t am0 = tig == 0 ? mn_lo0 : tig == 1 ? mn_hi0 : 0u, am1 = tig == 0 ? mn_lo1 : tig == 1 ? mn_hi1 : 0u;
+  int Ml[4], Mh[4];
+  mma_k32_uu(Ml, am0, am1, dw.x);
+  mma_k32_us(Mh, am0, am1, dw.y);
+  // |D| <= 32*15*127 = 60960 (low) / 16x that (high); x sc <= 63, 4 sub-blocks each: < 2.5e8.
+  int E00 = 0, E01 = 0, E10 = 0, E11 = 0, O00 = 0, O01 = 0, O10 = 0, O11 = 0;
 #pragma unroll
   for (int g = 0; g < 4; g++) {
     const uint32_t w[4] = {r.qs[g].x, r.qs[g].y, r.qs[g].z, r.qs[g].w};
 #pragma unroll
     for (int half = 0; half < 2; half++) {
       const int s = 2 * g + half;
-      const uint32_t aa[4] = {half ? (w[0] >> 4) & M4 : w[0] & M4, half ? (w[1] >> 4) & M4 : w[1] & M4,
-                              half ? (w[2] >> 4) & M4 : w[2] & M4, half ? (w[3] >> 4) & M4 : w[3] & M4};
-      const int sc0 = ubyte(s < 4 ? sc_lo0 : sc_hi0, s & 3), mn0 = ubyte(s < 4 ? mn_lo0 : mn_hi0, s & 3);
-      const int sc1 = ubyte(s < 4 ? sc_lo1 : sc_hi1, s & 3), mn1 = ubyte(s < 4 ? mn_lo1 : mn_hi1, s & 3);
+      const uint32_t m = half ? H4 : M4;
+      const uint32_t aa[4] = {w[0] & m, w[1] & m, w[2] & m, w[3] & m};
+      const int sc0 = ubyte(s < 4 ? sc_lo0 : sc_hi0, s & 3), sc1 = ubyte(s < 4 ? sc_lo1 : sc_hi1, s & 3);
       const uint4 bq = B[s >> 1];
       int D[4];
       mma_k32(D, aa, (s & 1) ? bq.z : bq.x, (s & 1) ? bq.w : bq.y);
-      const int4 dq = DS[s >> 1];
-      const int dx = (s & 1) ? dq.z : dq.x, dy = (s & 1) ? dq.w : dq.y;
-      // |D| <= 32*15*127 = 60960; x sc <= 63 and 8 sub-blocks: < 3.1e7. |dsum| <= 4064; x mn x 8 < 2.1e6.
-      I00 += sc0 * D[0];
-      I01 += sc0 * D[1];
-      I10 += sc1 * D[2];
-      I11 += sc1 * D[3];
-      M00 += mn0 * dx;
-      M01 += mn0 * dy;
-      M10 += mn1 * dx;
-      M11 += mn1 * dy;
+      if (half) {
+        O00 += sc0 * D[0];
+        O01 += sc0 * D[1];
+        O10 += sc1 * D[2];
+        O11 += sc1 * D[3];
+      } else {
+        E00 += sc0 * D[0];
+        E01 += sc0 * D[1];
+        E10 += sc1 * D[2];
+        E11 += sc1 * D[3];
+      }
     }
   }
+  const int I00 = E00 + (O00 >> 4), I01 = E01 + (O01 >> 4), I10 = E10 + (O10 >> 4), I11 = E11 + (O11 >> 4);
+  const int M00 = Ml[0] + (Mh[0] << 8), M01 = Ml[1] + (Mh[1] << 8), M10 = Ml[2] + (Mh[2] << 8), M11 = Ml[3] + (Mh[3] << 8);
   const float d0 = h2f(r.h0.x), d1 = h2f(r.h1.x), m0 = h2f(r.h0.x >> 16), m1 = h2f(r.h1.x >> 16);
   const float sx = X.sxs[kb];
   acc[0] = fmaf(sx, fmaf(P.w0, d0 * (float)I00 - m0 * (float)M00, P.w1 * (d0 * (float)I01 - m0 * (float)M01)), acc[0]);
   acc[1] = fmaf(sx, fmaf(P.w0, d1 * (float)I10 - m1 * (float)M10, P.w1 * (d1 * (float)I11 - m1 * (float)M11)), acc[1]);
 }
 
+// One Q6_K tile chunk: sum_j d*sc_j*(q-32) x = s*d*(sum_j sc_j*D_j - 32*sum_j sc_j*Sdig_j), the
+// second sum one k16 MMA whose A fragment is the row's raw int8 scale words (k = 16-run j).
 __device__ __forceinline__ void p_q6k(const uint8_t *c, int kb, const PX &X, const PLane &P, int lane, float (&acc)[2]) {
   Q6KRegs r;
 #pragma unroll
   for (int k = 0; k < 4; k++) r.ql[k] = *reinterpret_cast<const uint4 *>(c + 512 * k + 16 * lane);
   r.qh[0] = *reinterpret_cast<const uint4 *>(c + 2048 + 16 * lane);
   r.qh[1] = *reinterpret_cast<const uint4 *>(c + 2560 + 16 * lane);
-  const int grp = lane >> 2;
+  const int grp = lane >> 2, tig = lane & 3;
   r.s0 = *reinterpret_cast<const uint4 *>(c + 3072 + 16 * grp);
   r.s1 = *reinterpret_cast<const uint4 *>(c + 3072 + 16 * (grp + 8));
   r.d = (uint32_t)*reinterpret_cast<const uint16_t *>(c + 3328 + 2 * grp) |
@@ -345,10 +411,16 @@ __device__ __forceinline__ void p_q6k(const uint8_t *c, int kb, const PX &X, con
   const uint32_t M4 = 0x0F0F0F0Fu, T3 = 0x03030303u;
   const uint32_t sw0[4] = {r.s0.x, r.s0.y, r.s0.z, r.s0.w}, sw1[4] = {r.s1.x, r.s1.y, r.s1.z, r.s1.w};
   const uint4 *bp = reinterpret_cast<const uint4 *>(X.brec + (size_t)kb * 960 + P.boff);
-  const int4 *dsp = reinterpret_cast<const int4 *>(X.ds + (size_t)kb * 576 + P.tig * 144);
   uint4 B[4];
 #pragma unroll
   for (int i = 0; i < 4; i++) B[i] = bp[i];
+  const uint2 dw = *reinterpret_cast<const uint2 *>(X.dsw + (size_t)kb * 256 + lane * 8);
+  // offset term: A = the 16 int8 scales of rows grp / grp+8 (k = 16-run), this lane's 4 of them
+  const uint32_t as0 = tig == 0 ? sw0[0] : tig == 1 ? sw0[1] : tig == 2 ? sw0[2] : sw0[3];
+  const uint32_t as1 = tig == 0 ? sw1[0] : tig == 1 ? sw1[1] : tig == 2 ? sw1[2] : sw1[3];
+  int Tl[4], Th[4];
+  mma_k16_su(Tl, as0, as1, dw.x);
+  mma_k16_ss(Th, as0, as1, dw.y);
   int I00 = 0, I01 = 0, I10 = 0, I11 = 0;
 #pragma unroll
   for (int seg = 0; seg < 2; seg++) {
@@ -369,16 +441,19 @@ __device__ __forceinline__ void p_q6k(const uint8_t *c, int kb, const PX &X, con
         const uint32_t b0 = (j & 1) ? (h ? bq.w : bq.z) : (h ? bq.y : bq.x);
         int D[4];
         mma_k16(D, a0, a1, b0);
-        const int4 dq = dsp[s >> 1];
-        const int dx = (s & 1) ? dq.z : dq.x, dy = (s & 1) ? dq.w : dq.y;
-        // |D - 32*dsum| <= 16*32*127 = 65024; x |sc| <= 128 and 16 sub-blocks: < 1.4e8.
-        I00 += sc0 * (D[0] - 32 * dx);
-        I01 += sc0 * (D[1] - 32 * dy);
-        I10 += sc1 * (D[2] - 32 * dx);
-        I11 += sc1 * (D[3] - 32 * dy);
+        // |D| <= 16*63*127 = 128016; x |sc| <= 128 and 16 sub-blocks: < 2.7e8.
+        I00 += sc0 * D[0];
+        I01 += sc0 * D[1];
+        I10 += sc1 * D[2];
+        I11 += sc1 * D[3];
       }
     }
   }
+  // |T| <= 16*128*2032 = 4.2e6 per entry; 32*T well inside int32
+  I00 -= 32 * (Tl[0] + (Th[0] << 8));
+  I01 -= 32 * (Tl[1] + (Th[1] << 8));
+  I10 -= 32 * (Tl[2] + (Th[2] << 8));
+  I11 -= 32 * (Tl[3] + (Th[3] << 8));
   const float d0 = h2f(r.d), d1 = h2f(r.d >> 16);
   const float sx = X.sxs[kb];
   acc[0] = fmaf(sx, fmaf(P.w0, d0 * (float)I00, P.w1 * (d0 * (float)I01)), acc[0]);
@@ -685,14 +760,13 @@ __device__ bool mbar_wait(uint64_t *b, unsigned par, volatile int *stop, int *st
     }
   } acc_guard{t0};
 #endif
-  while (!mbar_test(b, par)) {
+  while (!mbar_try(b, par)) {
     if (*stop) return false;
     if (gtime() - t0 > P_TIMEOUT_NS) {
       atomicCAS(status, 0, 1);
       *stop = 1;
       return false;
     }
-    __nanosleep(32);
   }
   return true;
 }
@@ -904,7 +978,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
         }
         const bool q6 = pg.type == Q6_K;
         const PX X = px_carve(xs, pg.cols);
-        p_digitise(pg.x, pg.norm_w, pg.eps, pg.cols, q6, X, sh.red, warp, lane);
+        p_digitise(pg.x, pg.norm_w, pg.eps, pg.cols, q6, X, sh.red, sh.dsum[warp], warp, lane);
         bar_comp();
         if (tid == 0) P_TRACE(step, p, 1);
         const PLane PL = p_lane(lane);
@@ -912,7 +986,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
         int nu = u0 + warp, kb = nkb ? nu % nkb : 0;
         for (int s0 = u0; s0 < u1; s0 += k, g++) {
           const int s1 = min(u1, s0 + k), slot = g % R.ns, rs = g % P_RES_STAGES;
-          // this warp's chunks of the stage (at most one: k <= 16 = P_CWARPS), result kept in registers
+          // this warp's chunks of the stage (at most one: k <= P_CWARPS), result kept in registers
           float r[1][2] = {{0.f, 0.f}};
           int nmine = 0;
           const int first = nu;

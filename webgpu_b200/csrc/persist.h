@@ -71,7 +71,7 @@ struct PersistArgs {
   int l2_ahead;  // ring stages requested into L2 ahead of the shared-memory copies (0: none)
 };
 
-constexpr int P_CWARPS = 16;                // compute warps (+ one epilogue warp, one producer warp)
+constexpr int P_CWARPS = 14;                // compute warps (+ one epilogue warp, one producer warp)
 constexpr int P_THREADS = (P_CWARPS + 2) * 32;
 constexpr int P_SLOT_BYTES = 32256;        // 14 Q4_K or 9 Q6_K tile chunks
 
