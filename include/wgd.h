@@ -154,6 +154,10 @@ WGD_API int wgd_set_graphs(wgd_ctx *ctx, int enabled);
  * then run as one cooperative launch per call (all layers, LM head, argmax, token feedback) when the
  * model's shapes allow it; otherwise, or when disabled, they use the per-kernel path. */
 WGD_API int wgd_set_persistent(wgd_ctx *ctx, int enabled);
+/* Projections of Q4_K matrices for forward batches of at least min_batch rows run on the tcgen05
+ * tensor-core GEMM (wgd_op_gemm_tiled) instead of the GEMV; 0 turns it off. Default 16; takes
+ * effect only if the model was loaded with a batch size of 8 or more. */
+WGD_API int wgd_set_prefill_gemm(wgd_ctx *ctx, int min_batch);
 /* 1 when the persistent decode kernel is available for this model, 0 when not (the reason is
  * written to why[0..why_len)). */
 WGD_API int wgd_persistent_status(wgd_ctx *ctx, char *why, int why_len);
@@ -190,6 +194,15 @@ WGD_API int wgd_op_gemv_tiled(int ggml_type, int64_t rows, int64_t cols, const v
  * later calls allocate nothing. Calls on one device must not overlap in time: they share the scratch. */
 WGD_API int wgd_op_gemv_tiled_noalloc(int ggml_type, int64_t rows, int64_t cols, const void *tiled_dev, const float *x_dev,
                                       int batch, float *y_dev, void *stream);
+/* Prompt-batch product over tiled Q4_K weights on the tcgen05 tensor cores (the matmul shader,
+ * shaders.ts, for a batch of rows; engine.ts:217-251 runs it for every projection of a prefill
+ * batch): y[b * rows + r] = sum_c W[r][c] * x[b * cols + c] for b < batch, 1 <= batch <= 128.
+ * Weights exact in f16, activations split into two f16 terms, f32 accumulation: the result
+ * agrees with wgd_op_gemv_tiled to fp32 rounding. Asynchronous on `stream`;
+ * wgd_op_gemm_tiled_status reports (and clears) a pipeline wait that ran out on this device. */
+WGD_API int wgd_op_gemm_tiled(int ggml_type, int64_t rows, int64_t cols, const void *tiled_dev, const float *x_dev, int batch,
+                              float *y_dev, void *stream);
+WGD_API int wgd_op_gemm_tiled_status(int *status);
 /* RMSNorm of n rows (normShader, shaders.ts:84-97). */
 WGD_API int wgd_op_rmsnorm(const float *x_dev, const float *w_dev, int cols, int n, float eps, float *y_dev, void *stream);
 /* Q/K rotation (+ optional per-head RMS norm) of x[n][heads][hd] in place:

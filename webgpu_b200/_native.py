@@ -68,6 +68,7 @@ SIGNATURES = {
     "wgd_stats_get": (c_int, [c_void_p, ctypes.POINTER(StatsC)]),
     "wgd_set_graphs": (c_int, [c_void_p, c_int]),
     "wgd_set_persistent": (c_int, [c_void_p, c_int]),
+    "wgd_set_prefill_gemm": (c_int, [c_void_p, c_int]),
     "wgd_persistent_status": (c_int, [c_void_p, c_char_p, c_int]),
     "wgd_dev_row_bytes": (c_int64, [c_int, c_int64]),
     "wgd_op_repack": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
@@ -78,6 +79,8 @@ SIGNATURES = {
     "wgd_op_dequant_tiled": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "wgd_op_gemv_tiled": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "wgd_op_gemv_tiled_noalloc": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "wgd_op_gemm_tiled": (c_int, [c_int, c_int64, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "wgd_op_gemm_tiled_status": (c_int, [ctypes.POINTER(c_int)]),
     "wgd_op_rmsnorm": (c_int, [c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_void_p]),
     "wgd_op_rope": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_float, c_float, c_int, c_int, c_void_p]),
     "wgd_op_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_int,

@@ -138,6 +138,13 @@ struct wgd_ctx {
   size_t g2_part_floats = 0;
   unsigned *g2_ctr = nullptr;
   int g2_ctr_count = 0;
+  // prompt-batch tcgen05 GEMM (gemm_tc.cu): Q4_K projections of batches >= tc_min_batch
+  int tc_min_batch = 16;
+  int tc_cols_max = 0, tc_rows_max = 0;
+  uint8_t *tc_panel = nullptr;
+  float *tc_part = nullptr;
+  unsigned *tc_ctr = nullptr;
+  int *tc_status = nullptr;  // device address of h_io[IO_TC]
   int32_t *h_io = nullptr;  // pinned: [0] start, [1] argmax, [2..] ids
   // graph
   bool graphs = true;
@@ -171,8 +178,9 @@ struct wgd_ctx {
   uint8_t *reader_buf = nullptr;
   uint64_t reader_buf_bytes = 0;
 };
-// h_io slots: [0] start, [1] argmax, [2..1015] ids, [1016..1019] persistent status, [1020] cancel word
-constexpr int IO_STATUS = 1016, IO_CANCEL = 1020;
+// h_io slots: [0] start, [1] argmax, [2..1015] ids, [1016..1019] persistent status, [1020] cancel word,
+// [1021] tensor-core GEMM status
+constexpr int IO_STATUS = 1016, IO_CANCEL = 1020, IO_TC = 1021;
 
 // ------------------------------------------------------------------ helpers
 
@@ -276,6 +284,7 @@ wgd_ctx *wgd_create(int device, int tp_rank, int tp_size, uint64_t budget_bytes,
     delete ctx;
     return nullptr;
   }
+  memset(ctx->h_io, 0, sizeof(int32_t) * 1024);
   ctx->st.page_bytes = page_bytes;
   set(WGD_OK);
   return ctx;
@@ -396,6 +405,10 @@ static int alloc_linear(wgd_ctx *ctx, DevLinear &L, int type, int rows, int cols
     const size_t pf = gemv2_part_floats(type, rows, cols, ctx->sm_count);
     if (pf > ctx->g2_part_floats) ctx->g2_part_floats = pf;
     if ((rows + 15) / 16 > ctx->g2_ctr_count) ctx->g2_ctr_count = (rows + 15) / 16;
+    if (type == Q4_K) {
+      ctx->tc_cols_max = std::max(ctx->tc_cols_max, cols);
+      ctx->tc_rows_max = std::max(ctx->tc_rows_max, rows);
+    }
   }
   L.unit_rows = L.tiled ? TILE_ROWS : GEMV_ROWS;  // pages cut at whole tiles / whole gate|up interleave blocks
   L.label = label;
@@ -818,6 +831,13 @@ extern "C" int wgd_model_end(wgd_ctx *ctx) {
   if (ctx->g2_part_floats && ((rc = ctx_alloc_t(ctx, &ctx->g2_part, ctx->g2_part_floats, "gemv partials")) ||
                               (rc = ctx_alloc_t(ctx, &ctx->g2_ctr, (size_t)ctx->g2_ctr_count, "gemv tile counters"))))
     return rc;
+  if (ctx->tc_cols_max && B >= 8) {
+    if ((rc = ctx_alloc_t(ctx, &ctx->tc_panel, gemm_tc_panel_bytes(B, ctx->tc_cols_max), "GEMM activation panel")) ||
+        (rc = ctx_alloc_t(ctx, &ctx->tc_part, gemm_tc_part_floats(B, ctx->sm_count), "GEMM partials")) ||
+        (rc = ctx_alloc_t(ctx, &ctx->tc_ctr, (size_t)gemm_tc_mtiles(ctx->tc_rows_max), "GEMM counters")))
+      return rc;
+    CK(cudaHostGetDevicePointer((void **)&ctx->tc_status, ctx->h_io + IO_TC, 0));
+  }
   if (tp > 1) {
     if ((rc = tp_create(&ctx->tp, ctx->tp_rank, tp, (size_t)B * H, &g_err))) return rc;
   }
@@ -1003,6 +1023,28 @@ static int gemv_paged(wgd_ctx *ctx, const DevLinear &L, const float *x, int ldx,
 static int gemv(wgd_ctx *ctx, const DevLinear &L, const float *x, int ldx, const float *norm_w, float *y, int ldy,
                 const float *bias, int epi, int batch) {
   if (L.streamed) return gemv_paged(ctx, L, x, ldx, norm_w, y, ldy, bias, epi, batch);
+  if (L.tiled && L.type == Q4_K && ctx->tc_panel && ctx->tc_min_batch > 0 && batch >= ctx->tc_min_batch) {
+    GemmTcLaunch g{};
+    g.w = L.w;
+    g.rows = L.rows;
+    g.cols = L.cols;
+    g.x = x;
+    g.ldx = ldx;
+    g.norm_w = norm_w;
+    g.eps = ctx->c.epsilon;
+    g.y = y;
+    g.ldy = ldy;
+    g.bias = bias;
+    g.epi = epi;
+    g.batch = batch;
+    g.panel = ctx->tc_panel;
+    g.part = ctx->tc_part;
+    g.ctr = ctx->tc_ctr;
+    g.status = ctx->tc_status;
+    ctx->kernels += 2;  // activation panel + GEMM
+    CK(launch_gemm_tc(g, ctx->stream, ctx->sm_count));
+    return WGD_OK;
+  }
   const int chunk = L.tiled ? gemv2_max_batch(L.cols) : gemv_max_batch(L.cols);
   ctx->kernels += chunk > 0 ? (batch + chunk - 1) / chunk : 1;
   if (L.tiled) {
@@ -1216,6 +1258,10 @@ extern "C" int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, i
   ctx->st.tokens += n;
   if (ctx->tp && tp_failed(ctx->tp)) return fail(WGD_ETIMEOUT, "a tensor-parallel peer did not answer within the wait limit");
   if (persist && (rc = persist_status(ctx))) return rc;
+  if (ctx->h_io[IO_TC]) {
+    ctx->h_io[IO_TC] = 0;
+    return fail(WGD_ETIMEOUT, "a tensor-core GEMM pipeline wait ran out");
+  }
   if (want >= 1) {
     if (ctx->h_io[1] < 0) return fail(WGD_ENONFINITE, "Inference produced non-finite logits. Stop and report this model/runtime combination.");
     if (argmax_out) *argmax_out = ctx->h_io[1];
@@ -1331,6 +1377,13 @@ extern "C" int wgd_stats_get(wgd_ctx *ctx, wgd_stats *out) {
 extern "C" int wgd_set_graphs(wgd_ctx *ctx, int enabled) {
   if (!ctx) return fail(WGD_EINVAL, "null context");
   ctx->graphs = enabled != 0;
+  return WGD_OK;
+}
+
+extern "C" int wgd_set_prefill_gemm(wgd_ctx *ctx, int min_batch) {
+  if (!ctx) return fail(WGD_EINVAL, "null context");
+  if (min_batch < 0) return fail(WGD_EINVAL, "min_batch must be >= 0");
+  ctx->tc_min_batch = min_batch;
   return WGD_OK;
 }
 

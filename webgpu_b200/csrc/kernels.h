@@ -66,6 +66,36 @@ size_t gemv2_part_floats(int type, int rows, int cols, int sm_count);
 // Largest activation chunk per pass (0 if the width is unsupported).
 int gemv2_max_batch(int cols);
 
+// ------------------------------------------------ prompt-batch tensor-core GEMM
+// The same operation for a batch of activation rows on tcgen05 tensor cores
+// (Q4_K in the tile-16 layout; gemm_tc.cu). Scratch: `panel` holds the prepared
+// activations (gemm_tc_panel_bytes), `part` the partial sums of M-tiles cut
+// between CTAs (gemm_tc_part_floats), `ctr` gemm_tc_mtiles(rows) zeroed
+// counters (left zeroed). *status is set to 1 if a pipeline wait ran out.
+constexpr int GEMM_TC_MAX_BATCH = 128;
+struct GemmTcLaunch {
+  const uint8_t *w;
+  int rows, cols;
+  const float *x;
+  int ldx;
+  const float *norm_w;
+  float eps;
+  float *y;
+  int ldy;
+  const float *bias;
+  int epi;
+  int batch;
+  uint8_t *panel;
+  float *part;
+  unsigned *ctr;
+  int *status;
+};
+cudaError_t launch_gemm_tc(const GemmTcLaunch &a, cudaStream_t s, int sm_count);
+bool gemm_tc_supported(int type, int rows, int cols, int batch);
+size_t gemm_tc_panel_bytes(int batch, int cols);
+size_t gemm_tc_part_floats(int batch, int sm_count);
+int gemm_tc_mtiles(int rows);
+
 // --------------------------------------------------------------- layout
 // Raw GGUF rows -> device rows. Source rows [0, nrows) at `src` (row stride
 // `src_row_bytes`); block columns [blk0, blk0 + nbl) of each row are moved to
