@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 import oracle
-from webgpu_b200 import synth
+from webgpu_b200 import _native, synth
 from webgpu_b200.engine import PagedEngine
 from webgpu_b200.gguf import model_config, parse_gguf_header
 from webgpu_b200.source import MemorySource
@@ -161,11 +161,33 @@ def test_graph_replay_equals_eager(cuda):
 
 
 def test_budget_and_argument_errors(cuda):
+    """Weights beyond the budget are paged (test_gpu_pager); what must fit is the attention state
+    (checked by the host, gpu.ts:309-315 wording) and the fixed device buffers (checked by the
+    library: WGD_EBUDGET from model_end)."""
+    import ctypes
+
     from webgpu_b200._native import WgdError
+    from webgpu_b200.gguf import model_config, read_gguf, to_native_config
+    from webgpu_b200.source import MemorySource
     spec = synth.baseline_spec(3, layers=2)
-    with pytest.raises(WgdError) as ei:
-        load(spec, context=4096, batch=16, budget=1024)
-    assert "GPU budget exceeded" in str(ei.value)
+    image = synth.build_gguf(spec)
+    with pytest.raises(ValueError, match="attention state"):
+        load(spec, context=32768, batch=16, budget=600, image=image)
+    L = _native.lib()
+    g = read_gguf(MemorySource(image))
+    status = ctypes.c_int(0)
+    ctx = L.wgd_create(0, 0, 1, 96 << 20, 16 << 20, ctypes.byref(status))
+    assert ctx, status.value
+    try:
+        cfg = to_native_config(model_config(g))
+        _native.check(L.wgd_model_begin(ctx, ctypes.byref(cfg), 4096, 16))
+        for t in g.tensors.values():
+            dims = (ctypes.c_uint64 * 4)(*t.dims, *([0] * (4 - len(t.dims))))
+            _native.check(L.wgd_tensor_register(ctx, t.name.encode(), t.type, dims, len(t.dims), t.offset, t.bytes, t.row_bytes))
+        with pytest.raises(WgdError, match="GPU budget exceeded"):
+            _native.check(L.wgd_model_end(ctx))
+    finally:
+        L.wgd_destroy(ctx)
     e, _ = load(synth.baseline_spec(0), batch=8)
     with pytest.raises(WgdError, match="token id out of range"):
         e.forward([600], 0, True)

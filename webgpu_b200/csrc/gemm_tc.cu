@@ -93,7 +93,7 @@ __device__ __forceinline__ int unit_owner(const TcArgs &a, int u) {
 __device__ bool tc_wait(uint64_t *b, unsigned par, volatile int *stop, int *status) {
   if (mbar_test(b, par)) return true;
   const uint64_t t0 = gtime();
-  while (!mbar_try(b, par)) {
+  while (!mbar_try_sleep(b, par, 1000000u)) {
     if (*stop) return false;
     if (gtime() - t0 > TC_TIMEOUT_NS) {
       atomicCAS(status, 0, 1);
@@ -319,7 +319,7 @@ __device__ __forceinline__ void emit(const TcArgs &a, int row, int b, float v, i
 }
 
 __device__ void role_epilogue(const TcArgs &a, uint32_t tbase, const float *cscale, uint64_t *accfull, uint64_t *accempty,
-                              uint64_t *mnempty, volatile int *stop, volatile int *islast, int u0, int u1, int q, int lane) {
+                              uint64_t *mnempty, volatile int *stop, int *pend, int u0, int u1, int q, int lane) {
   const int N = a.N, m = 32 * q + lane;
   const uint32_t lt = tbase + ((uint32_t)(32 * q) << 16);
   const int cta = blockIdx.x;
@@ -380,32 +380,94 @@ __device__ void role_epilogue(const TcArgs &a, uint32_t tbase, const float *csca
       mbar_arrive(mnempty);
     }
     if (!last || whole) continue;
-    // M-tile cut between CTAs: the last of its contributors sums the partials in CTA order
+    // M-tile cut between CTAs: publish this CTA's partial (one arrival on the M-tile's
+    // counter); the contributors sum the partials at the end of their ranges (finalize)
     __threadfence();
     epi_bar();
-    const int c0 = unit_owner(a, mt * a.nkb), c1 = unit_owner(a, (mt + 1) * a.nkb - 1);
     if (q == 0 && lane == 0) {
-      int flag = 0;
-      if (!*stop) {
-        __threadfence();
-        const unsigned old = atomicAdd(a.ctr + mt, 1u);
-        flag = old == (unsigned)(c1 - c0);
-      }
-      *islast = flag;
+      atomicAdd(a.ctr + mt, 1u);
+      pend[slot] = mt;
     }
-    epi_bar();
-    if (*islast) {
-      __threadfence();
-      for (int bb = 0; bb < a.batch; bb++) {
-        float v = 0.f;
-        for (int cc = c0; cc <= c1; cc++) {
-          const int sl = unit_start(a, cc) >= mt * a.nkb ? 0 : 1;
-          v += __ldcg(a.part + ((size_t)(cc * 2 + sl) * N + bb) * TC_M + m);
+  }
+}
+
+// Output of 16 consecutive rows row0.. (one 16-row tile) of activation row b.
+__device__ void emit16(const TcArgs &a, int row0, int b, const float (&v)[16]) {
+  if (a.epi == EPI_GLU_SILU || a.epi == EPI_GLU_GELU) {
+    float *dst = a.y + (int64_t)b * a.ldy + (row0 >> 4) * 8;
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      if (row0 + j < a.rows) dst[j] = (a.epi == EPI_GLU_SILU ? tc_silu(v[j]) : tc_gelu(v[j])) * v[j + 8];
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 16; j++) {
+    const int row = row0 + j;
+    if (row >= a.rows) break;
+    float x = v[j];
+    if (a.bias) x += __ldg(a.bias + row);
+    float *dst = a.y + (int64_t)b * a.ldy + row;
+    if (a.epi == EPI_ADD) *dst += x;
+    else if (a.epi == EPI_SILU) *dst = tc_silu(x);
+    else *dst = x;
+  }
+}
+
+// M-tile mt was cut between CTAs c0..c1: once all of them have published their
+// partials, CTA c0 + i sums (in CTA order) and writes activation rows
+// [i*batch/C, (i+1)*batch/C) of it; the last to finish resets the counter.
+// Whole CTA; every thread reaches both block barriers.
+__device__ void finalize(const TcArgs &a, int mt, volatile int *stop) {
+  const int c0 = unit_owner(a, mt * a.nkb), c1 = unit_owner(a, (mt + 1) * a.nkb - 1), C = c1 - c0 + 1;
+  const int me = (int)blockIdx.x - c0;
+  if (threadIdx.x == 0 && !*stop) {
+    const uint64_t t0 = gtime();
+    while (ld_acquire(a.ctr + mt) < (unsigned)C) {
+      if (gtime() - t0 > TC_TIMEOUT_NS) {
+        atomicCAS(a.status, 0, 1);
+        *stop = 1;
+        break;
+      }
+      __nanosleep(100);
+    }
+  }
+  __syncthreads();
+  if (!*stop) {
+    const int b0 = me * a.batch / C, b1 = (me + 1) * a.batch / C, items = (b1 - b0) * TC_TILES;
+    for (int it = threadIdx.x; it < items; it += blockDim.x) {
+      const int b = b0 + it / TC_TILES, t = it % TC_TILES;
+      float acc[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++) acc[j] = 0.f;
+      for (int cc = c0; cc <= c1; cc += 4) {
+        float4 v[4][4];
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+          if (cc + g > c1) break;
+          const int sl = unit_start(a, cc + g) >= mt * a.nkb ? 0 : 1;
+          const float4 *src = reinterpret_cast<const float4 *>(a.part + ((size_t)((cc + g) * 2 + sl) * a.N + b) * TC_M + 16 * t);
+#pragma unroll
+          for (int k = 0; k < 4; k++) v[g][k] = __ldcg(src + k);
         }
-        emit(a, row, bb, v, lane);
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+          if (cc + g > c1) break;
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            acc[4 * k] += v[g][k].x;
+            acc[4 * k + 1] += v[g][k].y;
+            acc[4 * k + 2] += v[g][k].z;
+            acc[4 * k + 3] += v[g][k].w;
+          }
+        }
       }
-      if (q == 0 && lane == 0) a.ctr[mt] = 0u;
+      emit16(a, mt * TC_M + 16 * t, b, acc);
     }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !*stop) {
+    const unsigned old = atomicAdd(a.ctr + mt, 1u);
+    if (old == (unsigned)(2 * C - 1)) atomicExch(a.ctr + mt, 0u);
   }
 }
 
@@ -417,7 +479,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs a) 
   static_assert((3 * TC_MAXST + 10) * 8 <= 384, "barrier area");
   uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + 384);
   volatile int *stop = reinterpret_cast<volatile int *>(smem + 388);
-  volatile int *islast = reinterpret_cast<volatile int *>(smem + 392);
+  int *pend = reinterpret_cast<int *>(smem + 392);  // M-tiles of this CTA's cut segments (first, last) or -1
   float *cscale = reinterpret_cast<float *>(smem + 512);  // N <= 128 floats
   uint8_t *raw = smem + TC_HDR;
   uint8_t *stages = raw + 2 * TC_RAW_BYTES;
@@ -439,7 +501,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs a) 
     mbar_init(mnempty, 4);
     mbar_init(drain, 1);
     *stop = 0;
-    *islast = 0;
+    pend[0] = pend[1] = -1;
     fence_async_smem();
   }
   if (threadIdx.x < a.N)
@@ -456,7 +518,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs a) 
   if (warp < TC_DQ) {
     role_dequant(a, raw, stages, afull, empty, rawfull, rawempty, stop, u0, u1, warp, lane);
   } else if (warp < TC_EPI0 + 4) {
-    role_epilogue(a, tbase, cscale, accfull, accempty, mnempty, stop, islast, u0, u1, warp - TC_EPI0, lane);
+    role_epilogue(a, tbase, cscale, accfull, accempty, mnempty, stop, pend, u0, u1, warp - TC_EPI0, lane);
   } else if (warp == TC_RAWW) {
     if (lane == 0) role_raw(a, raw, rawfull, rawempty, stop, u0, u1);
   } else if (warp == TC_BW) {
@@ -469,6 +531,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs a) 
   __syncthreads();
   tc_fence_after();
   if (warp == TC_MMAW) tmem_dealloc(tbase, a.tmem_cols);
+  // cut M-tiles: the first segment's tile, then the last's (each CTA waits only for
+  // contributors that publish before they finalize, so the waits cannot cycle)
+  const int p0 = pend[0], p1 = pend[1];
+  if (p0 >= 0) finalize(a, p0, stop);
+  if (p1 >= 0) finalize(a, p1, stop);
 }
 
 // One block per activation row (N rows, rows >= batch are zero): optional

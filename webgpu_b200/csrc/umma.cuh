@@ -62,10 +62,27 @@ __device__ __forceinline__ bool mbar_try(uint64_t *b, unsigned parity) {
       : "memory");
   return ok != 0;
 }
+// Suspends the thread until the phase completes or `hint_ns` passes (then false):
+// waiting threads then take no issue slots or shared-memory bandwidth from the
+// warps doing the work.
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t *b, unsigned parity, unsigned hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ uint64_t gtime() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 // Bulk copy global -> this CTA's shared memory, completing on mbarrier `bar`
 // (both addresses 16-byte aligned, size a multiple of 16).

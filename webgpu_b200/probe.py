@@ -4,6 +4,8 @@
     python -m webgpu_b200.probe gemv ROWS COLS TYPE [LAUNCHES]   # wgd_op_gemv_tiled on random blocks
     python -m webgpu_b200.probe attention                        # wgd_op_attention, decode, L = 512/2048/4096
     python -m webgpu_b200.probe decode LAYERS STEPS [PERSISTENT]  # Llama-3-8B-width model, wgd_decode
+    python -m webgpu_b200.probe gemm ROWS COLS BATCH [LAUNCHES]  # wgd_op_gemm_tiled (Q4_K) vs the GEMV
+    python -m webgpu_b200.probe prefill LAYERS BATCH [MIN_BATCH]  # Llama-3-8B-width prompt batches
 
 `gemv` repacks random GGUF blocks of TYPE (12 = Q4_K, 14 = Q6_K) into the tile layout once and calls the
 tiled GEMV LAUNCHES times (default 5). `attention` keeps 24 K/V caches of [8][4096][128] fp32 (more than
@@ -90,6 +92,64 @@ def decode(layers: int, steps: int, persistent: int = 1) -> None:
     e.dispose()
 
 
+def gemm(rows: int, cols: int, batch: int, launches: int = 20) -> None:
+    """Times the tcgen05 GEMM and the tiled GEMV on one Q4_K matrix (CUDA events; the weights
+    of 8 copies rotate so that every launch reads them from HBM when they exceed L2)."""
+    import torch
+    L = _native.lib()
+    nb = L.wgd_tiled_bytes(12, rows, cols)
+    copies = max(1, min(8, (1 << 30) // nb))
+    raw = synth.random_blocks(12, rows * cols // 256, 2, 99)
+    rd = torch.from_numpy(raw).cuda()
+    mats = []
+    for _ in range(copies):
+        m = torch.empty(nb + 16, dtype=torch.uint8, device="cuda")
+        _native.check(L.wgd_op_repack_tiled(12, rows, cols, rd.data_ptr(), m.data_ptr(), None))
+        mats.append(m)
+    x = torch.randn(batch * cols, device="cuda")
+    y = torch.empty(batch * rows, device="cuda")
+    flops = 2.0 * rows * cols * batch
+    for name, fn in (("gemm_tc", L.wgd_op_gemm_tiled), ("gemv_tiled", L.wgd_op_gemv_tiled)):
+        for i in range(3):
+            _native.check(fn(12, rows, cols, mats[i % copies].data_ptr(), x.data_ptr(), batch, y.data_ptr(), None))
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        for i in range(launches):
+            _native.check(fn(12, rows, cols, mats[i % copies].data_ptr(), x.data_ptr(), batch, y.data_ptr(), None))
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / launches * 1000
+        print(f"{name} Q4_K {rows}x{cols} batch {batch}: {us:8.2f} us/launch  {flops / us / 1e6:8.1f} TFLOP/s "
+              f"(f16 MMA work x2: {2 * flops / us / 1e6:8.1f})  weights {nb / us / 1e3:7.1f} GB/s", flush=True)
+    st = ctypes.c_int(0)
+    _native.check(L.wgd_op_gemm_tiled_status(ctypes.byref(st)))
+    assert st.value == 0
+
+
+def prefill(layers: int, batch: int, min_batch: int = 16) -> None:
+    """Prefill of 512 tokens in batches of BATCH through wgd_forward (Llama-3-8B widths)."""
+    from .engine import PagedEngine
+    from .source import MemorySource
+    spec = synth.baseline_spec(3, layers=layers)
+    img = synth.build_gguf(spec)
+    e = PagedEngine()
+    e.load(MemorySource(img), {"contextLength": 4096, "batchSize": batch, "performance": "fast", "gpuBudgetMiB": 100000})
+    L = _native.lib()
+    _native.check(L.wgd_set_prefill_gemm(e.ctx, min_batch))
+    prompt = list(synth.uniform_ids(512, 128256, seed=2))
+    st = _native.StatsC()
+    for rep in range(3):
+        total = 0.0
+        for i in range(0, 512, batch):
+            e.forward(prompt[i:i + batch], i, i + batch == 512)
+            _native.check(L.wgd_stats_get(e.ctx, ctypes.byref(st)))
+            total += st.last_forward_ms
+        print(f"prefill layers {layers} batch {batch} min_batch {min_batch}: {total:.2f} ms for 512 tokens "
+              f"({512 / total * 1000:.0f} tok/s)", flush=True)
+    e.dispose()
+
+
 def main(argv):
     if not argv:
         print(__doc__)
@@ -101,6 +161,10 @@ def main(argv):
         attention(*args)
     elif cmd == "decode":
         decode(*args)
+    elif cmd == "gemm":
+        gemm(*args)
+    elif cmd == "prefill":
+        prefill(*args)
     else:
         print(__doc__)
         return 2
