@@ -34,6 +34,8 @@
 //                       activations), or as a partial that the CTA arriving
 //                       last for that M-tile sums in CTA order (deterministic).
 // Tensor memory columns: [0,N) R0, [N,2N) R1, [2N,3N) Mn, [3N,4N) Y.
+// Within a CTA's M-tile segment the super-blocks start at a per-CTA rotation, so
+// that CTAs running at the same time read different parts of the panel.
 // Every mbarrier wait is bounded (2 s of globaltimer); a wait that runs out
 // sets *status = 1 and the CTA winds down (copies and MMAs in flight are
 // waited for, tensor memory is freed).
@@ -52,8 +54,11 @@ constexpr int TC_M = 128;                            // weight rows per M-tile
 constexpr int TC_TILES = TC_M / TILE_ROWS;           // tiles per M-tile
 constexpr int TC_CHUNK = 2304;                       // Q4_K tile chunk (16 rows x 144 B)
 constexpr int TC_DQ = 8;                             // dequant warps 0..7 (one tile each)
-constexpr int TC_EPI0 = 8;                           // epilogue warps 8..11 (lane quarters 0..3)
-constexpr int TC_RAWW = 12, TC_BW = 13, TC_MMAW = 14;
+constexpr int TC_EPI0 = 8;                           // epilogue warps 8..11: TMEM lane quarters 0..3
+constexpr int TC_EPIW = 4;
+constexpr int TC_RAWW = 12, TC_BW = 13, TC_MMAW = 14;  // single-lane roles (the MMA warp also owns the tensor memory)
+// Registers are handed out per group of 4 warps: 15 warps cost 16 warps' worth, at
+// most 128 per thread.
 constexpr int TC_THREADS = 15 * 32;
 constexpr int TC_A_BYTES = TC_M * 64 * 2;            // A of one 64-column stage
 constexpr int TC_AMIN_BYTES = TC_M * 16 * 2;         // mins operand
@@ -88,6 +93,24 @@ struct TcArgs {
 __device__ __forceinline__ int unit_start(const TcArgs &a, int c) { return c * a.q + (c < a.rem ? c : a.rem); }
 __device__ __forceinline__ int unit_owner(const TcArgs &a, int u) {
   return u < a.thr ? u / (a.q + 1) : a.rem + (u - a.thr) / a.q;
+}
+
+// The unit at position U of this CTA's range [u0, u1): the range is cut into M-tile
+// segments, and each segment's super-blocks are visited from a per-CTA rotation on
+// (kb0 + (j + rot) mod len), so that CTAs running at the same time read different
+// parts of the activation panel. j is the position inside the segment.
+struct UnitPos {
+  int mt, kb, j, len;
+};
+__device__ __forceinline__ UnitPos unit_pos(const TcArgs &a, int u0, int u1, int U) {
+  UnitPos p;
+  p.mt = U / a.nkb;
+  const int seg0 = max(u0, p.mt * a.nkb), seg1 = min(u1, (p.mt + 1) * a.nkb);
+  p.len = seg1 - seg0;
+  p.j = U - seg0;
+  const int rot = (int)((blockIdx.x * 7u) % (unsigned)p.len);
+  p.kb = seg0 - p.mt * a.nkb + (p.j + rot) % p.len;
+  return p;
 }
 
 __device__ bool tc_wait(uint64_t *b, unsigned par, volatile int *stop, int *status) {
@@ -172,7 +195,8 @@ __device__ void role_raw(const TcArgs &a, uint8_t *raw, uint64_t *rawfull, uint6
                          int u1) {
   int i = 0;
   for (int U = u0; U < u1; U++, i++) {
-    const int mt = U / a.nkb, kb = U - mt * a.nkb, r = i & 1;
+    const UnitPos P = unit_pos(a, u0, u1, U);
+    const int mt = P.mt, kb = P.kb, r = i & 1;
     if (!tc_wait(rawempty + r, ((i >> 1) & 1) ^ 1, stop, a.status)) break;
     const int n = min(TC_TILES, a.tiles - mt * TC_TILES);
     mbar_expect_tx(rawfull + r, (unsigned)(n * TC_CHUNK));
@@ -187,7 +211,7 @@ __device__ void role_b(const TcArgs &a, uint8_t *stages, uint64_t *bfull, uint64
   const int N = a.N;
   unsigned G = 0;
   for (int U = u0; U < u1; U++) {
-    const int kb = U % a.nkb;
+    const int kb = unit_pos(a, u0, u1, U).kb;
     for (int g = 0; g < 4; g++, G++) {
       const int s = G % a.nstage;
       if (!tc_wait(empty + s, ((G / a.nstage) & 1) ^ 1, stop, a.status)) goto done;
@@ -300,77 +324,116 @@ done:
   tc_drain(drain, 0);
 }
 
-// Final value of (global row, activation row b): the epilogue operation.
-// Every lane of the warp calls it with the same b (gated rows read their up row
-// from lane + 8).
-__device__ __forceinline__ void emit(const TcArgs &a, int row, int b, float v, int lane) {
-  if (a.epi == EPI_GLU_SILU || a.epi == EPI_GLU_GELU) {
+// Final value of (global row, activation row b) through the epilogue operation
+// (bias `brow` already loaded for the row). Every lane of the warp calls it with the
+// same b (gated rows read their up row from lane + 8).
+template <int EPI>
+__device__ __forceinline__ void emit(const TcArgs &a, int row, int b, float v, float brow, int lane) {
+  if constexpr (EPI == EPI_GLU_SILU || EPI == EPI_GLU_GELU) {
     const float u = __shfl_down_sync(0xffffffffu, v, 8);
     if ((lane & 8) == 0 && row < a.rows)
-      a.y[(int64_t)b * a.ldy + (row >> 4) * 8 + (row & 7)] = (a.epi == EPI_GLU_SILU ? tc_silu(v) : tc_gelu(v)) * u;
-    return;
+      a.y[(int64_t)b * a.ldy + (row >> 4) * 8 + (row & 7)] = (EPI == EPI_GLU_SILU ? tc_silu(v) : tc_gelu(v)) * u;
+  } else {
+    if (row >= a.rows) return;
+    float *dst = a.y + (int64_t)b * a.ldy + row;
+    if constexpr (EPI == EPI_ADD) *dst += v + brow;
+    else if constexpr (EPI == EPI_SILU) *dst = tc_silu(v + brow);
+    else *dst = v + brow;
   }
-  if (row >= a.rows) return;
-  if (a.bias) v += __ldg(a.bias + row);
-  float *dst = a.y + (int64_t)b * a.ldy + row;
-  if (a.epi == EPI_ADD) *dst += v;
-  else if (a.epi == EPI_SILU) *dst = tc_silu(v);
-  else *dst = v;
 }
 
+// Y = Y + d*R - dmin*Mn for columns c..c+15 of this thread's row (Y absent on the
+// first unit of a segment), then either kept in tensor memory or written out.
+// (in place: r becomes the new Y, as float bits)
+__device__ __forceinline__ void epi_cols16(uint32_t (&r)[16], const uint32_t (&mn)[16], const uint32_t (&yv)[16], bool first, float d,
+                                           float dmin) {
+#pragma unroll
+  for (int j = 0; j < 16; j++)
+    r[j] = __float_as_uint((first ? 0.f : __uint_as_float(yv[j])) + fmaf(d, __uint_as_float(r[j]), -dmin * __uint_as_float(mn[j])));
+}
+
+template <int EPI>
+__device__ __forceinline__ void out_cols16(const TcArgs &a, const uint32_t (&v)[16], const float *cscale, int c, bool whole, int row,
+                                           float brow, int lane, float *pdst) {
+  float cs[16];
+#pragma unroll
+  for (int j = 0; j < 16; j += 4) {
+    const float4 t = *reinterpret_cast<const float4 *>(cscale + c + j);
+    cs[j] = t.x;
+    cs[j + 1] = t.y;
+    cs[j + 2] = t.z;
+    cs[j + 3] = t.w;
+  }
+  if (whole) {
+#pragma unroll
+    for (int j = 0; j < 16; j++)
+      if (c + j < a.batch) emit<EPI>(a, row, c + j, __uint_as_float(v[j]) * cs[j], brow, lane);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; j++)
+      if (c + j < a.batch) pdst[(size_t)(c + j) * TC_M] = __uint_as_float(v[j]) * cs[j];
+  }
+}
+
+template <int EPI>
 __device__ void role_epilogue(const TcArgs &a, uint32_t tbase, const float *cscale, uint64_t *accfull, uint64_t *accempty,
-                              uint64_t *mnempty, volatile int *stop, int *pend, int u0, int u1, int q, int lane) {
+                              uint64_t *mnempty, volatile int *stop, int *pend, int u0, int u1, int q, int h, int lane) {
   const int N = a.N, m = 32 * q + lane;
+  // this warp's 16-column chunks (h: which half of them when two warps share a lane quarter)
+  const int nch = N / 16, half = TC_EPIW == 8 ? (nch + 1) / 2 : nch;
+  const int cbeg = h ? 16 * half : 0, cend = h ? N : 16 * half;
   const uint32_t lt = tbase + ((uint32_t)(32 * q) << 16);
   const int cta = blockIdx.x;
   int i = 0;
   for (int U = u0; U < u1; U++, i++) {
-    const int mt = U / a.nkb, kb = U - mt * a.nkb, b = i & 1;
-    const bool first = U == u0 || kb == 0, last = U == u1 - 1 || kb == a.nkb - 1;
-    const int seg0 = max(u0, mt * a.nkb), seg1 = min(u1, (mt + 1) * a.nkb);
-    const bool whole = seg0 == mt * a.nkb && seg1 == (mt + 1) * a.nkb;
+    const UnitPos P = unit_pos(a, u0, u1, U);
+    const int mt = P.mt, kb = P.kb, b = i & 1;
+    const bool first = P.j == 0, last = P.j == P.len - 1, whole = P.len == a.nkb;
     const int row = mt * TC_M + m, tile = mt * TC_TILES + (m >> 4);
     uint32_t hdr = 0;
     if (tile < a.tiles) hdr = ldg_u32(a.w + ((size_t)tile * a.nkb + kb) * TC_CHUNK + 2048 + 16 * (m & 15));
+    float brow = 0.f;
+    if (last && whole && a.bias && row < a.rows) brow = __ldg(a.bias + row);
     bool ok = tc_wait(accfull + b, (i >> 1) & 1, stop, a.status);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     const float d = h2f(hdr), dmin = h2f(hdr >> 16);
     const int slot = u0 >= mt * a.nkb ? 0 : 1;
-    for (int c = 0; c < N; c += 16) {
-      uint32_t r[16], mn[16], yv[16];
+    float *pdst = a.part + (size_t)(cta * 2 + slot) * N * TC_M + m;
+    for (int c = cbeg; c < cend; c += 16) {
+      const bool two = false;  // (32 columns per round trip need more registers than this block has)
+      uint32_t r0[16], m0[16], y0[16], r1[16], m1[16], y1[16];
       if (ok) {
-        tmem_ld16(lt + b * N + c, r);
-        tmem_ld16(lt + 2 * N + c, mn);
-        if (!first) tmem_ld16(lt + 3 * N + c, yv);
+        tmem_ld16(lt + b * N + c, r0);
+        tmem_ld16(lt + 2 * N + c, m0);
+        if (!first) tmem_ld16(lt + 3 * N + c, y0);
+        if (two) {
+          tmem_ld16(lt + b * N + c + 16, r1);
+          tmem_ld16(lt + 2 * N + c + 16, m1);
+          if (!first) tmem_ld16(lt + 3 * N + c + 16, y1);
+        }
         tmem_wait_ld();
-        reg_fence(r);
-        reg_fence(mn);
-        if (!first) reg_fence(yv);
+        reg_fence(r0);
+        reg_fence(m0);
+        reg_fence(y0);
+        reg_fence(r1);
+        reg_fence(m1);
+        reg_fence(y1);
       } else {
 #pragma unroll
-        for (int j = 0; j < 16; j++) r[j] = mn[j] = yv[j] = 0u;
+        for (int j = 0; j < 16; j++) r0[j] = m0[j] = y0[j] = r1[j] = m1[j] = y1[j] = 0u;
       }
-      float v[16];
-#pragma unroll
-      for (int j = 0; j < 16; j++)
-        v[j] = (first ? 0.f : __uint_as_float(yv[j])) + fmaf(d, __uint_as_float(r[j]), -dmin * __uint_as_float(mn[j]));
+      epi_cols16(r0, m0, y0, first, d, dmin);
+      epi_cols16(r1, m1, y1, first, d, dmin);
       if (!last) {
         if (ok) {
-#pragma unroll
-          for (int j = 0; j < 16; j++) yv[j] = __float_as_uint(v[j]);
-          tmem_st16(lt + 3 * N + c, yv);
+          tmem_st16(lt + 3 * N + c, r0);
+          if (two) tmem_st16(lt + 3 * N + c + 16, r1);
         }
         continue;
       }
-#pragma unroll
-      for (int j = 0; j < 16; j++) {
-        const int bb = c + j;
-        if (bb >= a.batch) break;
-        const float val = v[j] * cscale[bb];
-        if (whole) emit(a, row, bb, val, lane);
-        else a.part[((size_t)(cta * 2 + slot) * N + bb) * TC_M + m] = val;
-      }
+      out_cols16<EPI>(a, r0, cscale, c, whole, row, brow, lane, pdst);
+      if (two) out_cols16<EPI>(a, r1, cscale, c + 16, whole, row, brow, lane, pdst);
     }
     if (!last && ok) tmem_wait_st();
     tc_fence_before();
@@ -384,7 +447,7 @@ __device__ void role_epilogue(const TcArgs &a, uint32_t tbase, const float *csca
     // counter); the contributors sum the partials at the end of their ranges (finalize)
     __threadfence();
     epi_bar();
-    if (q == 0 && lane == 0) {
+    if (q == 0 && h == 0 && lane == 0) {
       atomicAdd(a.ctr + mt, 1u);
       pend[slot] = mt;
     }
@@ -392,24 +455,25 @@ __device__ void role_epilogue(const TcArgs &a, uint32_t tbase, const float *csca
 }
 
 // Output of 16 consecutive rows row0.. (one 16-row tile) of activation row b.
+template <int EPI>
 __device__ void emit16(const TcArgs &a, int row0, int b, const float (&v)[16]) {
-  if (a.epi == EPI_GLU_SILU || a.epi == EPI_GLU_GELU) {
+  if constexpr (EPI == EPI_GLU_SILU || EPI == EPI_GLU_GELU) {
     float *dst = a.y + (int64_t)b * a.ldy + (row0 >> 4) * 8;
 #pragma unroll
     for (int j = 0; j < 8; j++)
-      if (row0 + j < a.rows) dst[j] = (a.epi == EPI_GLU_SILU ? tc_silu(v[j]) : tc_gelu(v[j])) * v[j + 8];
-    return;
-  }
+      if (row0 + j < a.rows) dst[j] = (EPI == EPI_GLU_SILU ? tc_silu(v[j]) : tc_gelu(v[j])) * v[j + 8];
+  } else {
 #pragma unroll
-  for (int j = 0; j < 16; j++) {
-    const int row = row0 + j;
-    if (row >= a.rows) break;
-    float x = v[j];
-    if (a.bias) x += __ldg(a.bias + row);
-    float *dst = a.y + (int64_t)b * a.ldy + row;
-    if (a.epi == EPI_ADD) *dst += x;
-    else if (a.epi == EPI_SILU) *dst = tc_silu(x);
-    else *dst = x;
+    for (int j = 0; j < 16; j++) {
+      const int row = row0 + j;
+      if (row >= a.rows) break;
+      float x = v[j];
+      if (a.bias) x += __ldg(a.bias + row);
+      float *dst = a.y + (int64_t)b * a.ldy + row;
+      if constexpr (EPI == EPI_ADD) *dst += x;
+      else if constexpr (EPI == EPI_SILU) *dst = tc_silu(x);
+      else *dst = x;
+    }
   }
 }
 
@@ -417,6 +481,7 @@ __device__ void emit16(const TcArgs &a, int row0, int b, const float (&v)[16]) {
 // partials, CTA c0 + i sums (in CTA order) and writes activation rows
 // [i*batch/C, (i+1)*batch/C) of it; the last to finish resets the counter.
 // Whole CTA; every thread reaches both block barriers.
+template <int EPI>
 __device__ void finalize(const TcArgs &a, int mt, volatile int *stop) {
   const int c0 = unit_owner(a, mt * a.nkb), c1 = unit_owner(a, (mt + 1) * a.nkb - 1), C = c1 - c0 + 1;
   const int me = (int)blockIdx.x - c0;
@@ -439,10 +504,10 @@ __device__ void finalize(const TcArgs &a, int mt, volatile int *stop) {
       float acc[16];
 #pragma unroll
       for (int j = 0; j < 16; j++) acc[j] = 0.f;
-      for (int cc = c0; cc <= c1; cc += 4) {
-        float4 v[4][4];
+      for (int cc = c0; cc <= c1; cc += 2) {
+        float4 v[2][4];
 #pragma unroll
-        for (int g = 0; g < 4; g++) {
+        for (int g = 0; g < 2; g++) {
           if (cc + g > c1) break;
           const int sl = unit_start(a, cc + g) >= mt * a.nkb ? 0 : 1;
           const float4 *src = reinterpret_cast<const float4 *>(a.part + ((size_t)((cc + g) * 2 + sl) * a.N + b) * TC_M + 16 * t);
@@ -450,7 +515,7 @@ __device__ void finalize(const TcArgs &a, int mt, volatile int *stop) {
           for (int k = 0; k < 4; k++) v[g][k] = __ldcg(src + k);
         }
 #pragma unroll
-        for (int g = 0; g < 4; g++) {
+        for (int g = 0; g < 2; g++) {
           if (cc + g > c1) break;
 #pragma unroll
           for (int k = 0; k < 4; k++) {
@@ -461,7 +526,7 @@ __device__ void finalize(const TcArgs &a, int mt, volatile int *stop) {
           }
         }
       }
-      emit16(a, mt * TC_M + 16 * t, b, acc);
+      emit16<EPI>(a, mt * TC_M + 16 * t, b, acc);
     }
   }
   __syncthreads();
@@ -471,6 +536,7 @@ __device__ void finalize(const TcArgs &a, int mt, volatile int *stop) {
   }
 }
 
+template <int EPI>
 __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t *bfull = reinterpret_cast<uint64_t *>(smem), *afull = bfull + TC_MAXST, *empty = afull + TC_MAXST, *rawfull = empty + TC_MAXST,
@@ -496,9 +562,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs a) 
       mbar_init(rawfull + r, 1);
       mbar_init(rawempty + r, TC_DQ);
       mbar_init(accfull + r, 1);
-      mbar_init(accempty + r, 4);
+      mbar_init(accempty + r, TC_EPIW);
     }
-    mbar_init(mnempty, 4);
+    mbar_init(mnempty, TC_EPIW);
     mbar_init(drain, 1);
     *stop = 0;
     pend[0] = pend[1] = -1;
@@ -517,8 +583,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs a) 
 
   if (warp < TC_DQ) {
     role_dequant(a, raw, stages, afull, empty, rawfull, rawempty, stop, u0, u1, warp, lane);
-  } else if (warp < TC_EPI0 + 4) {
-    role_epilogue(a, tbase, cscale, accfull, accempty, mnempty, stop, pend, u0, u1, warp - TC_EPI0, lane);
+  } else if (warp < TC_EPI0 + TC_EPIW) {
+    role_epilogue<EPI>(a, tbase, cscale, accfull, accempty, mnempty, stop, pend, u0, u1, warp & 3, 0, lane);
   } else if (warp == TC_RAWW) {
     if (lane == 0) role_raw(a, raw, rawfull, rawempty, stop, u0, u1);
   } else if (warp == TC_BW) {
@@ -534,8 +600,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs a) 
   // cut M-tiles: the first segment's tile, then the last's (each CTA waits only for
   // contributors that publish before they finalize, so the waits cannot cycle)
   const int p0 = pend[0], p1 = pend[1];
-  if (p0 >= 0) finalize(a, p0, stop);
-  if (p1 >= 0) finalize(a, p1, stop);
+  if (p0 >= 0) finalize<EPI>(a, p0, stop);
+  if (p1 >= 0) finalize<EPI>(a, p1, stop);
 }
 
 // One block per activation row (N rows, rows >= batch are zero): optional
@@ -692,13 +758,25 @@ cudaError_t launch_gemm_tc(const GemmTcLaunch &L, cudaStream_t s, int sm_count) 
   a.rem = units % grid;
   a.thr = a.rem * (a.q + 1);
   const size_t smem = (size_t)TC_HDR + 2 * TC_RAW_BYTES + (size_t)a.nstage * a.sbytes;
-  static bool attr = false;
-  if (!attr) {
-    e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_MAX);
-    if (e != cudaSuccess) return e;
-    attr = true;
+  void (*kern)(const TcArgs) = nullptr;
+  switch (L.epi) {
+    case EPI_STORE: kern = gemm_tc_kernel<EPI_STORE>; break;
+    case EPI_ADD: kern = gemm_tc_kernel<EPI_ADD>; break;
+    case EPI_SILU: kern = gemm_tc_kernel<EPI_SILU>; break;
+    case EPI_GLU_SILU: kern = gemm_tc_kernel<EPI_GLU_SILU>; break;
+    case EPI_GLU_GELU: kern = gemm_tc_kernel<EPI_GLU_GELU>; break;
+    default: return cudaErrorInvalidValue;
   }
-  gemm_tc_kernel<<<grid, TC_THREADS, smem, s>>>(a);
+  static bool attr[5] = {false, false, false, false, false};
+  if (!attr[L.epi]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_MAX);
+    if (e != cudaSuccess) return e;
+    cudaFuncAttributes fa;
+    if ((e = cudaFuncGetAttributes(&fa, kern)) != cudaSuccess) return e;
+    if (fa.maxThreadsPerBlock < TC_THREADS) return cudaErrorLaunchOutOfResources;  // register budget of the build
+    attr[L.epi] = true;
+  }
+  kern<<<grid, TC_THREADS, smem, s>>>(a);
   return cudaGetLastError();
 }
 
