@@ -15,9 +15,12 @@ batches of 128 (untimed), then decode steps from position 512.
   e2e    tokens/s through the per-token C-ABI call (wgd_forward) with the token
          id copied in from pinned host memory and the greedy id read back every
          step, wall clock around the loop, max over ranks.
-  roofline  the dominant kernel (the fused gate|up Q4_K GEMV, 28672 x 4096)
-         timed in this process with CUDA events over weight copies larger than
-         L2, algorithmic bytes / average launch time vs the measured HBM peak.
+  roofline  the persistent decode kernel over whole steps: algorithmic bytes
+         per step (weights + KV) / step time vs the measured HBM peak; the
+         stand-alone gate|up Q4_K GEMV (28672 x 4096) as gemv_probe.
+  prefill  the 512-token prompt prefilled again in batches of 128 (device
+         time, max over ranks): every Q4_K projection runs on the tcgen05
+         GEMM; projection TFLOP/s against the measured bf16 tensor peak.
   cpu_baseline  the CPU restatement of the reference decoder (oracle/, float64)
          on a bounded sample of the same model, rank 0 only.
 
@@ -59,6 +62,22 @@ def peaks():
         d = json.load(open(p))
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def tensor_peak():
+    """Dense bf16 TFLOP/s (burst) of MEASURED_PEAKS.json, else the fallback figure."""
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+def projection_flops(c, tokens: int, world: int) -> float:
+    """2 * tokens * (elements of every layer projection) / world: the prefill GEMM work."""
+    H, hd = c.hidden, c.head_dim
+    q, kv = c.heads * hd, c.kv_heads * hd
+    per_layer = H * (q + 2 * kv) + q * H + 2 * H * c.intermediate + c.intermediate * H
+    return 2.0 * tokens * per_layer * c.layers / world
 
 
 def log(*a):
@@ -310,6 +329,18 @@ def main():
     prefill_s = time.perf_counter() - t0
     pos = len(prompt)
 
+    # ---- prefill again, device time (the tcgen05 GEMM carries every Q4_K projection of a
+    # 128-row batch); the same tokens rewrite the same KV rows
+    barrier()
+    pf_ms = 0.0
+    for i in range(0, len(prompt), PREFILL_BATCH):
+        chunk = prompt[i:i + PREFILL_BATCH]
+        eng.forward(chunk, i, i + len(chunk) == len(prompt))
+        stp = _native.StatsC()
+        L.wgd_stats_get(eng.ctx, ctypes.byref(stp))
+        pf_ms += stp.last_forward_ms
+    pf_ms = max_over_ranks(pf_ms)
+
     # warm-up of both paths
     buf = (ctypes.c_int32 * max(args.steps, args.warmup))()
     _native.check(L.wgd_decode(eng.ctx, tok, pos, args.warmup, buf), "decode")
@@ -366,6 +397,20 @@ def main():
                 "traffic": STEP_TRAFFIC if persistent else None, "launch_ms": dev_ms, "steps_per_launch": args.steps,
                 "gemv_probe": probe}
 
+    prefill = None
+    if rank == 0:
+        tpk, tpk_kind = tensor_peak()
+        pf_flops = projection_flops(c, len(prompt), world)
+        pf_tflops = pf_flops / (pf_ms / 1000.0) / 1e12
+        prefill = {"tokens": len(prompt), "batch": PREFILL_BATCH, "ms": pf_ms, "tok_per_s": len(prompt) / (pf_ms / 1000.0),
+                   "kernel": "gemm_tc_kernel (tcgen05.mma kind::f16 M128 N128, TMEM accumulators) for every Q4_K projection",
+                   "projection_tflops": pf_tflops, "tensor_peak": tpk, "tensor_peak_kind": f"{tpk_kind} (bf16_tflops)",
+                   "frac": pf_tflops / tpk,
+                   "tensor_work_frac": 2 * pf_tflops / tpk,
+                   "note": "whole forward (projections, attention, rope, norms) timed; FLOPs count the projections only; "
+                           "tensor work is twice the algorithmic FLOPs (activation hi/lo split); ncu tensor-pipe "
+                           "utilisation of the GEMM kernel: profiles/gemm_tc_q4k_28672x4096_b128.md"}
+
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = cpu_threads()
@@ -384,7 +429,7 @@ def main():
                        "l2": "weights (4.36 GB) exceed L2 every step", "rope": "adjacent-pair (llama GGUF rule)",
                        "layers": c.layers, "prefill_s": prefill_s},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 + 4, "d2h_bytes_per_step": 4},
-            "roofline": roof, "cpu_baseline": base, "clocks": clocks,
+            "roofline": roof, "cpu_baseline": base, "clocks": clocks, "prefill": prefill,
             "gpu_launches": launches,
             "tokens_match_e2e": tokens_dev == tokens_e2e,
         }
