@@ -545,6 +545,217 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnArgs a
   pdl_launch_dependents();
 }
 
+// Prompt-batch attention (n > 1 rows, no fused RoPE): one CTA per (block of
+// ATR_ROWS consecutive query rows, kv head, key split) stages each K/V tile
+// once for all ATR_ROWS * G query heads of the block (the decode kernel above
+// would read every tile once per row). Warp w owns query-head vectors
+// qh = w + 8i (qh = row * G + head); lane j scores key j of the tile with the
+// row's causal window as mask; the online softmax and the PV accumulation are
+// the decode kernel's, per vector. Splits of at least ATR_MIN_CHUNK keys are
+// merged by the CTA of the block that arrives last (same partial layout).
+constexpr int ATR_ROWS = 8, ATR_THREADS = 256, ATR_WARPS = 8, ATR_MIN_CHUNK = 512;
+
+template <int NI>
+__global__ void __launch_bounds__(ATR_THREADS, 1) attention_rows_kernel(const AttnArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  const int G = a.heads / a.kv_heads, hd = a.hd, hd4 = hd >> 2, RS = hd + 4;
+  const int QH = ATR_ROWS * G;
+  float *q_s = sm;             // [QH][hd]
+  float *kv_s = q_s + QH * hd; // [2][K|V][ATT_TILE][RS]
+  __shared__ int last_s;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int qb = blockIdx.x / a.kv_heads, kh = blockIdx.x % a.kv_heads, sp = blockIdx.y;
+  pdl_wait();
+  const int start = a.start ? *a.start : a.start_host;
+  const int t0 = qb * ATR_ROWS, nrows = min(ATR_ROWS, a.n - t0);
+  // the block's key range: from the first row's window start to the last row's position
+  const int end_first = start + t0 + 1, kmin = end_first - (end_first < a.window ? end_first : a.window);
+  const int kmax = start + t0 + nrows, L = kmax - kmin;
+  int chunk = (L + a.splits - 1) / a.splits;
+  if (chunk < ATR_MIN_CHUNK) chunk = ATR_MIN_CHUNK;
+  const int nsp = (L + chunk - 1) / chunk;
+  if (sp >= nsp) return;
+  const int p0 = kmin + sp * chunk, p1 = min(kmax, p0 + chunk);
+  const float *kb = a.k + (int64_t)kh * a.capacity * hd;
+  const float *vb = a.v + (int64_t)kh * a.capacity * hd;
+  const int ntiles = (p1 - p0 + ATT_TILE - 1) / ATT_TILE;
+
+  auto stage = [&](int tile, int st) {
+    const int cnt = min(ATT_TILE, p1 - tile), total = cnt * hd4;
+    float *ks = kv_s + (size_t)st * 2 * ATT_TILE * RS, *vs = ks + ATT_TILE * RS;
+    for (int i = tid; i < total; i += ATR_THREADS) {
+      const int r = i / hd4, c = (i - r * hd4) * 4;
+      const int64_t row = (int64_t)((tile + r) % a.capacity) * hd;
+      cp_async16(ks + r * RS + c, kb + row + c);
+      cp_async16(vs + r * RS + c, vb + row + c);
+    }
+    cp_async_commit();
+  };
+  stage(p0, 0);
+  if (ntiles > 1) stage(p0 + ATT_TILE, 1);
+  for (int i = tid; i < QH * hd4; i += ATR_THREADS) {
+    const int qh = i / hd4, d4 = i - qh * hd4, r = qh / G, g = qh - r * G;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < nrows) v = reinterpret_cast<const float4 *>(a.q + ((int64_t)(t0 + r) * a.heads + kh * G + g) * hd)[d4];
+    reinterpret_cast<float4 *>(q_s + qh * hd)[d4] = v;
+  }
+
+  // this warp's vectors: qh = warp + 8i, i < G (row r = qh / G); row r's keys are
+  // [P_r + 1 - min(P_r + 1, window), P_r] with P_r = start + t0 + r
+  float m[ATT_GMAX], l[ATT_GMAX];
+  float4 acc[ATT_GMAX][NI];
+  int lo[ATT_GMAX], hi[ATT_GMAX];
+#pragma unroll
+  for (int i = 0; i < ATT_GMAX; i++) {
+    m[i] = -FLT_MAX;
+    l[i] = 0.f;
+#pragma unroll
+    for (int k = 0; k < NI; k++) acc[i][k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int qh = warp + ATR_WARPS * i, r = qh / G;
+    const int P = start + t0 + r, e = P + 1;
+    hi[i] = r < nrows ? P : -1;  // dead vectors (past the last row) match no key
+    lo[i] = e - (e < a.window ? e : a.window);
+  }
+
+  for (int ti = 0; ti < ntiles; ti++) {
+    const int tile = p0 + ti * ATT_TILE, cnt = min(ATT_TILE, p1 - tile), st = ti & 1;
+    if (ti + 1 < ntiles) cp_async_wait<1>(); else cp_async_wait<0>();
+    __syncthreads();
+    const float *ks = kv_s + (size_t)st * 2 * ATT_TILE * RS, *vs = ks + ATT_TILE * RS;
+    const int key = tile + lane;
+    float sc[ATT_GMAX];
+#pragma unroll
+    for (int i = 0; i < ATT_GMAX; i++) sc[i] = 0.f;
+    {
+      const float4 *kr = reinterpret_cast<const float4 *>(ks + lane * RS);
+#pragma unroll 4
+      for (int d4 = 0; d4 < hd4; d4++) {
+        const float4 k4 = kr[d4];
+#pragma unroll
+        for (int i = 0; i < ATT_GMAX; i++) {
+          if (i < G) {
+            const float4 q = reinterpret_cast<const float4 *>(q_s + (warp + ATR_WARPS * i) * hd)[d4];
+            sc[i] = fmaf(q.x, k4.x, fmaf(q.y, k4.y, fmaf(q.z, k4.z, fmaf(q.w, k4.w, sc[i]))));
+          }
+        }
+      }
+    }
+    float e[ATT_GMAX];
+#pragma unroll
+    for (int i = 0; i < ATT_GMAX; i++) {
+      e[i] = 0.f;
+      if (i < G) {
+        const bool live = lane < cnt && key >= lo[i] && key <= hi[i];
+        const float s_ = live ? sc[i] * a.scale : -FLT_MAX;
+        const float mn = fmaxf(m[i], warp_max(s_)), corr = expf(m[i] - mn);
+        e[i] = live ? expf(s_ - mn) : 0.f;
+        l[i] = fmaf(l[i], corr, warp_sum(e[i]));
+        m[i] = mn;
+#pragma unroll
+        for (int k = 0; k < NI; k++) acc[i][k] = make_float4(acc[i][k].x * corr, acc[i][k].y * corr, acc[i][k].z * corr, acc[i][k].w * corr);
+      }
+    }
+#pragma unroll 2
+    for (int j = 0; j < cnt; j++) {
+      const float4 *vr = reinterpret_cast<const float4 *>(vs + j * RS);
+      float4 v[NI];
+#pragma unroll
+      for (int k = 0; k < NI; k++) {
+        const int d4 = lane + 32 * k;
+        v[k] = d4 < hd4 ? vr[d4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < ATT_GMAX; i++) {
+        if (i < G) {
+          const float w = __shfl_sync(0xffffffffu, e[i], j);
+#pragma unroll
+          for (int k = 0; k < NI; k++) acc[i][k] = f4_fma(w, v[k], acc[i][k]);
+        }
+      }
+    }
+    __syncthreads();  // stage st is free again
+    if (ti + 2 < ntiles) stage(tile + 2 * ATT_TILE, st);
+  }
+
+  const int PR = hd + 4;
+  if (nsp == 1) {
+#pragma unroll
+    for (int i = 0; i < ATT_GMAX; i++) {
+      const int qh = warp + ATR_WARPS * i, r = qh / G, g = qh - r * G;
+      if (i >= G || r >= nrows) continue;
+      float *o = a.out + ((int64_t)(t0 + r) * a.heads + kh * G + g) * hd;
+#pragma unroll
+      for (int k = 0; k < NI; k++) {
+        const int d4 = lane + 32 * k;
+        if (d4 < hd4)
+          reinterpret_cast<float4 *>(o)[d4] = make_float4(acc[i][k].x / l[i], acc[i][k].y / l[i], acc[i][k].z / l[i], acc[i][k].w / l[i]);
+      }
+    }
+    pdl_launch_dependents();
+    return;
+  }
+  // partial rows: [(row * kv_heads + kh) * splits + sp][g] of acc | m | l | pad
+#pragma unroll
+  for (int i = 0; i < ATT_GMAX; i++) {
+    const int qh = warp + ATR_WARPS * i, r = qh / G, g = qh - r * G;
+    if (i >= G || r >= nrows) continue;
+    float *part = a.part + (((int64_t)(t0 + r) * a.kv_heads + kh) * a.splits + sp) * G * PR + g * PR;
+#pragma unroll
+    for (int k = 0; k < NI; k++) {
+      const int d4 = lane + 32 * k;
+      if (d4 < hd4) reinterpret_cast<float4 *>(part)[d4] = acc[i][k];
+    }
+    if (lane == 0) {
+      part[hd] = m[i];
+      part[hd + 1] = l[i];
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  const int pair = qb * a.kv_heads + kh;
+  if (tid == 0) last_s = atomicAdd(a.ctr + pair, 1u) == (unsigned)(nsp - 1);
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  const int64_t sstride = (int64_t)G * PR;
+  for (int qh = warp; qh < nrows * G; qh += ATR_WARPS) {
+    const int r = qh / G, g = qh - r * G;
+    const float *ph = a.part + ((int64_t)(t0 + r) * a.kv_heads + kh) * a.splits * sstride + g * PR;
+    const float ma = lane < nsp ? __ldcg(ph + lane * sstride + hd) : -FLT_MAX;
+    const float mb = lane + 32 < nsp ? __ldcg(ph + (lane + 32) * sstride + hd) : -FLT_MAX;
+    const float M = warp_max(fmaxf(ma, mb));
+    const float wa = lane < nsp ? expf(ma - M) : 0.f, wb = lane + 32 < nsp ? expf(mb - M) : 0.f;
+    const float la = lane < nsp ? __ldcg(ph + lane * sstride + hd + 1) : 0.f;
+    const float lb = lane + 32 < nsp ? __ldcg(ph + (lane + 32) * sstride + hd + 1) : 0.f;
+    const float den = warp_sum(fmaf(wa, la, wb * lb));
+    float *o = a.out + ((int64_t)(t0 + r) * a.heads + kh * G + g) * hd;
+#pragma unroll
+    for (int k = 0; k < NI; k++) {
+      const int d4 = lane + 32 * k;
+      float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < nsp; j++) {
+        const float w = __shfl_sync(0xffffffffu, j < 32 ? wa : wb, j & 31);
+        if (d4 < hd4) num = f4_fma(w, __ldcg(reinterpret_cast<const float4 *>(ph + j * sstride) + d4), num);
+      }
+      if (d4 < hd4) reinterpret_cast<float4 *>(o)[d4] = make_float4(num.x / den, num.y / den, num.z / den, num.w / den);
+    }
+  }
+  if (tid == 0) a.ctr[pair] = 0u;
+  pdl_launch_dependents();
+}
+
+template <int NI>
+static cudaError_t launch_attention_rows_ni(const AttnArgs &a, size_t smem, cudaStream_t s, bool pdl) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attention_rows_kernel<NI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int blocks = (a.n + ATR_ROWS - 1) / ATR_ROWS;
+  return launch_k(attention_rows_kernel<NI>, dim3(blocks * a.kv_heads, a.splits), dim3(ATR_THREADS), smem, s, pdl, a);
+}
+
 template <int NI>
 static cudaError_t launch_attention_ni(const AttnArgs &a, size_t smem, cudaStream_t s, bool pdl) {
   static bool attr = false;
@@ -562,6 +773,11 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
   if ((reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.out) |
        reinterpret_cast<uintptr_t>(a.part)) & 15)
     return cudaErrorMisalignedAddress;
+  if (a.n > 1 && !a.qkv && a.hd <= 256) {  // prompt batch: K/V tiles shared by ATR_ROWS query rows
+    const size_t smem = sizeof(float) * ((size_t)ATR_ROWS * G * a.hd + 2 * 2 * ATT_TILE * (size_t)(a.hd + 4));
+    if (a.hd <= 128) return launch_attention_rows_ni<1>(a, smem, s, pdl);
+    return launch_attention_rows_ni<2>(a, smem, s, pdl);
+  }
   const int nst = a.hd <= 256 ? 2 : 1;
   const size_t smem = sizeof(float) * ((size_t)G * a.hd + 2 * (size_t)a.hd + (size_t)nst * 2 * ATT_TILE * (a.hd + 4));
   if (a.hd <= 128) return launch_attention_ni<1>(a, smem, s, pdl);
