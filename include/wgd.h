@@ -154,7 +154,7 @@ WGD_API int wgd_set_graphs(wgd_ctx *ctx, int enabled);
  * then run as one cooperative launch per call (all layers, LM head, argmax, token feedback) when the
  * model's shapes allow it; otherwise, or when disabled, they use the per-kernel path. */
 WGD_API int wgd_set_persistent(wgd_ctx *ctx, int enabled);
-/* Projections of Q4_K matrices for forward batches of at least min_batch rows run on the tcgen05
+/* Projections of Q4_K/Q6_K matrices for forward batches of at least min_batch rows run on the tcgen05
  * tensor-core GEMM (wgd_op_gemm_tiled) instead of the GEMV; 0 turns it off. Default 16; takes
  * effect only if the model was loaded with a batch size of 8 or more. */
 WGD_API int wgd_set_prefill_gemm(wgd_ctx *ctx, int min_batch);
@@ -194,7 +194,7 @@ WGD_API int wgd_op_gemv_tiled(int ggml_type, int64_t rows, int64_t cols, const v
  * later calls allocate nothing. Calls on one device must not overlap in time: they share the scratch. */
 WGD_API int wgd_op_gemv_tiled_noalloc(int ggml_type, int64_t rows, int64_t cols, const void *tiled_dev, const float *x_dev,
                                       int batch, float *y_dev, void *stream);
-/* Prompt-batch product over tiled Q4_K weights on the tcgen05 tensor cores (the matmul shader,
+/* Prompt-batch product over tiled Q4_K / Q6_K weights on the tcgen05 tensor cores (the matmul shader,
  * shaders.ts, for a batch of rows; engine.ts:217-251 runs it for every projection of a prefill
  * batch): y[b * rows + r] = sum_c W[r][c] * x[b * cols + c] for b < batch, 1 <= batch <= 128.
  * Weights exact in f16, activations split into two f16 terms, f32 accumulation: the result

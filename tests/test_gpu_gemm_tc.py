@@ -1,5 +1,5 @@
 """The prompt-batch tcgen05 GEMM (wgd_op_gemm_tiled) against the CPU oracle and
-against the integer tensor-core GEMV on the same tiled Q4_K weights.
+against the integer tensor-core GEMV on the same tiled Q4_K / Q6_K weights.
 
 Shapes are the quantised-GEMM microbench ones (4096x4096, 14336x4096, 4096x14336
 at batch 8/32/128) plus ragged cases: a last 16-row tile and a last 128-row
@@ -18,21 +18,21 @@ from webgpu_b200 import _native, synth
 from test_gpu_ops import near, tiled_on_device, to_dev
 
 pytestmark = pytest.mark.gpu
-Q4K = 12
+Q4K, Q6K = 12, 14
 
 
-def _gemm(torch, tiled, rows, cols, xd, batch):
+def _gemm(torch, tiled, rows, cols, xd, batch, ttype=Q4K):
     y = torch.full((batch * rows,), float("nan"), dtype=torch.float32, device="cuda")
-    _native.check(_native.lib().wgd_op_gemm_tiled(Q4K, rows, cols, tiled.data_ptr(), xd.data_ptr(), batch, y.data_ptr(), None))
+    _native.check(_native.lib().wgd_op_gemm_tiled(ttype, rows, cols, tiled.data_ptr(), xd.data_ptr(), batch, y.data_ptr(), None))
     st = ctypes.c_int(-1)
     _native.check(_native.lib().wgd_op_gemm_tiled_status(ctypes.byref(st)))
     assert st.value == 0, "a pipeline wait ran out"
     return y.cpu().numpy().reshape(batch, rows)
 
 
-def _gemv(torch, tiled, rows, cols, xd, batch):
+def _gemv(torch, tiled, rows, cols, xd, batch, ttype=Q4K):
     y = torch.empty(batch * rows, dtype=torch.float32, device="cuda")
-    _native.check(_native.lib().wgd_op_gemv_tiled(Q4K, rows, cols, tiled.data_ptr(), xd.data_ptr(), batch, y.data_ptr(), None))
+    _native.check(_native.lib().wgd_op_gemv_tiled(ttype, rows, cols, tiled.data_ptr(), xd.data_ptr(), batch, y.data_ptr(), None))
     torch.cuda.synchronize()
     return y.cpu().numpy().reshape(batch, rows)
 
@@ -90,7 +90,29 @@ def test_gemm_zero_and_large_rows(cuda):
         assert np.max(np.abs(got[r] - exp[r])) <= 1e-5 * s, (r, np.max(np.abs(got[r] - exp[r])) / s)
 
 
+@pytest.mark.parametrize("rows,cols,batch,with_oracle", [
+    (4096, 4096, 32, True), (4096, 4096, 128, False), (4096, 14336, 128, False), (1000, 4096, 17, True), (300, 512, 33, True),
+    (37, 256, 5, True), (2048, 5376, 64, True)])
+def test_gemm_q6k_matches_oracle_and_gemv(cuda, rows, cols, batch, with_oracle):
+    """Q6_K: A = sc*(q-32) as two exact f16 terms (even part and last bit of the scale), four MMAs per K-step."""
+    torch = cuda
+    raw = synth.random_blocks(Q6K, rows * cols // 256, seed=27, stream=Q6K)
+    x = synth.normal(batch * cols, 28, 3)
+    tiled = tiled_on_device(torch, Q6K, raw, rows, cols)
+    xd = to_dev(torch, x)
+    got = _gemm(torch, tiled, rows, cols, xd, batch, Q6K)
+    assert np.all(np.isfinite(got))
+    ref = _gemv(torch, tiled, rows, cols, xd, batch, Q6K)
+    scale = max(1.0, float(np.max(np.abs(ref))))
+    assert np.max(np.abs(got - ref)) <= 1e-4 * scale, np.max(np.abs(got - ref)) / scale
+    if with_oracle:
+        exp = oracle.matmul(raw, Q6K, rows, cols, x, batch)
+        near(got, exp)
+        # exact weights: relative error at the level of the fp32 sums, not of f16
+        assert np.max(np.abs(got - exp)) <= 1e-5 * max(1.0, float(np.max(np.abs(exp))))
+
+
 def test_gemm_rejects_unsupported_shapes(cuda):
     L = _native.lib()
-    for t, rows, cols, batch in [(14, 64, 256, 8), (Q4K, 64, 300, 8), (Q4K, 64, 256, 0), (Q4K, 64, 256, 129)]:
+    for t, rows, cols, batch in [(13, 64, 256, 8), (Q4K, 64, 300, 8), (Q4K, 64, 256, 0), (Q4K, 64, 256, 129)]:
         assert L.wgd_op_gemm_tiled(t, rows, cols, 1, 1, batch, 1, None) != 0

@@ -138,7 +138,7 @@ struct wgd_ctx {
   size_t g2_part_floats = 0;
   unsigned *g2_ctr = nullptr;
   int g2_ctr_count = 0;
-  // prompt-batch tcgen05 GEMM (gemm_tc.cu): Q4_K projections of batches >= tc_min_batch
+  // prompt-batch tcgen05 GEMM (gemm_tc.cu): Q4_K/Q6_K projections of batches >= tc_min_batch
   int tc_min_batch = 16;
   int tc_cols_max = 0, tc_rows_max = 0;
   uint8_t *tc_panel = nullptr;
@@ -405,10 +405,8 @@ static int alloc_linear(wgd_ctx *ctx, DevLinear &L, int type, int rows, int cols
     const size_t pf = gemv2_part_floats(type, rows, cols, ctx->sm_count);
     if (pf > ctx->g2_part_floats) ctx->g2_part_floats = pf;
     if ((rows + 15) / 16 > ctx->g2_ctr_count) ctx->g2_ctr_count = (rows + 15) / 16;
-    if (type == Q4_K) {
-      ctx->tc_cols_max = std::max(ctx->tc_cols_max, cols);
-      ctx->tc_rows_max = std::max(ctx->tc_rows_max, rows);
-    }
+    ctx->tc_cols_max = std::max(ctx->tc_cols_max, cols);  // tiled types (Q4_K, Q6_K) have a prompt-batch GEMM
+    ctx->tc_rows_max = std::max(ctx->tc_rows_max, rows);
   }
   L.unit_rows = L.tiled ? TILE_ROWS : GEMV_ROWS;  // pages cut at whole tiles / whole gate|up interleave blocks
   L.label = label;
@@ -1023,8 +1021,10 @@ static int gemv_paged(wgd_ctx *ctx, const DevLinear &L, const float *x, int ldx,
 static int gemv(wgd_ctx *ctx, const DevLinear &L, const float *x, int ldx, const float *norm_w, float *y, int ldy,
                 const float *bias, int epi, int batch) {
   if (L.streamed) return gemv_paged(ctx, L, x, ldx, norm_w, y, ldy, bias, epi, batch);
-  if (L.tiled && L.type == Q4_K && ctx->tc_panel && ctx->tc_min_batch > 0 && batch >= ctx->tc_min_batch) {
+  if (L.tiled && ctx->tc_panel && ctx->tc_min_batch > 0 && batch >= ctx->tc_min_batch &&
+      gemm_tc_supported(L.type, L.rows, L.cols, batch)) {
     GemmTcLaunch g{};
+    g.type = L.type;
     g.w = L.w;
     g.rows = L.rows;
     g.cols = L.cols;

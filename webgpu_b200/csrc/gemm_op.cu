@@ -47,7 +47,7 @@ extern "C" int wgd_op_gemm_tiled(int type, int64_t rows, int64_t cols, const voi
   if (!tiled || !x || !y) return api_fail(WGD_EINVAL, "null argument");
   if (rows < 1 || rows > (1 << 24) || cols < 256 || cols > (1 << 20) ||
       !gemm_tc_supported(type, (int)rows, (int)cols, batch))
-    return api_fail(WGD_EINVAL, "the tensor-core GEMM takes Q4_K, whole super-blocks and 1..128 activation rows");
+    return api_fail(WGD_EINVAL, "the tensor-core GEMM takes Q4_K or Q6_K, whole super-blocks and 1..128 activation rows");
   int dev = 0;
   CKG(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return api_fail(WGD_EINVAL, "device index");
@@ -84,6 +84,7 @@ extern "C" int wgd_op_gemm_tiled(int type, int64_t rows, int64_t cols, const voi
     }
   }
   GemmTcLaunch g{};
+  g.type = type;
   g.w = (const uint8_t *)tiled;
   g.rows = (int)rows;
   g.cols = (int)cols;

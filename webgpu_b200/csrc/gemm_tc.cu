@@ -1,5 +1,5 @@
 // Prompt-batch GEMM on the 5th-generation tensor cores (tcgen05 + tensor
-// memory) for Q4_K weights in the tile-16 layout (tile.cuh):
+// memory) for Q4_K and Q6_K weights in the tile-16 layout (tile.cuh):
 //   y[b][row] (op)= sum_k W[row][k] * x[b][k],   b < batch <= 128,
 // the operation of the reference's matmul shader for a prompt batch
 // (shaders.ts matmul over `batchSize` rows, driven by engine.ts:217-251).
@@ -13,6 +13,8 @@
 // gives Mn = sum_j mn_j * S_j with S_j = sum of x over sub-block j (also split
 // hi/lo), and the epilogue applies the super-block scales in fp32:
 //   y += d*R - dmin*Mn.
+// Q6_K (d*sc*(q-32), no mins): A is two exact f16 terms (see role_dequant<Q6_K>),
+// four MMAs per K-step (A_hi, A_lo against x_hi, x_lo), y += d*R.
 // Each activation row is scaled by a power of two first (max |x| in [512, 1024))
 // so that x_hi, x_lo and S stay inside the f16 range; the epilogue undoes it.
 //
@@ -52,7 +54,6 @@ using namespace tc;
 
 constexpr int TC_M = 128;                            // weight rows per M-tile
 constexpr int TC_TILES = TC_M / TILE_ROWS;           // tiles per M-tile
-constexpr int TC_CHUNK = 2304;                       // Q4_K tile chunk (16 rows x 144 B)
 constexpr int TC_DQ = 8;                             // dequant warps 0..7 (one tile each)
 constexpr int TC_EPI0 = 8;                           // epilogue warps 8..11: TMEM lane quarters 0..3
 constexpr int TC_EPIW = 4;
@@ -62,7 +63,6 @@ constexpr int TC_RAWW = 12, TC_BW = 13, TC_MMAW = 14;  // single-lane roles (the
 constexpr int TC_THREADS = 15 * 32;
 constexpr int TC_A_BYTES = TC_M * 64 * 2;            // A of one 64-column stage
 constexpr int TC_AMIN_BYTES = TC_M * 16 * 2;         // mins operand
-constexpr int TC_RAW_BYTES = TC_TILES * TC_CHUNK;    // one unit of raw weights
 constexpr int TC_HDR = 1024;                         // barriers, words, column scales
 constexpr int TC_MAXST = 8;
 constexpr int TC_SMEM_MAX = 232448;                  // 227 KB opt-in
@@ -71,7 +71,22 @@ constexpr uint64_t TC_TIMEOUT_NS = 2000000000ull;
 // Panel (prepared activations) per super-block: 4 stages of [hi N x 64][lo N x 64]
 // f16, then the sums operand [N x 16] f16; after all super-blocks, N f32 column scales.
 __host__ __device__ inline size_t panel_kb_bytes(int N) { return (size_t)N * 1056; }
-__host__ __device__ inline uint32_t stage_bytes(int N) { return (uint32_t)(TC_A_BYTES + TC_AMIN_BYTES + N * 288); }
+// Per weight type: tile chunk bytes, and the stage layout after A: Q4_K keeps the
+// 128 x 16 mins operand there, Q6_K the low part of its two-term A.
+template <int T> struct TcType;
+template <> struct TcType<Q4_K> {
+  static constexpr int CHUNK = 2304, A2 = TC_AMIN_BYTES;
+  static constexpr bool MINS = true;
+};
+template <> struct TcType<Q6_K> {
+  static constexpr int CHUNK = 3360, A2 = TC_A_BYTES;
+  static constexpr bool MINS = false;
+};
+__host__ __device__ inline int tc_chunk(int type) { return type == Q4_K ? 2304 : 3360; }
+__host__ __device__ inline int raw_bytes(int type) { return TC_TILES * tc_chunk(type); }
+__host__ __device__ inline uint32_t stage_bytes(int type, int N) {
+  return type == Q4_K ? (uint32_t)(TC_A_BYTES + TC_AMIN_BYTES + N * 288) : (uint32_t)(2 * TC_A_BYTES + N * 256);
+}
 
 struct TcArgs {
   const uint8_t *w;
@@ -191,22 +206,24 @@ __device__ __forceinline__ void sc_pair(uint32_t sc, uint32_t &s2, uint32_t &n2)
 
 // ------------------------------------------------------------------ roles
 
+template <int T>
 __device__ void role_raw(const TcArgs &a, uint8_t *raw, uint64_t *rawfull, uint64_t *rawempty, volatile int *stop, int u0,
                          int u1) {
+  constexpr int CH = TcType<T>::CHUNK, RAW = TC_TILES * CH;
   int i = 0;
   for (int U = u0; U < u1; U++, i++) {
     const UnitPos P = unit_pos(a, u0, u1, U);
     const int mt = P.mt, kb = P.kb, r = i & 1;
     if (!tc_wait(rawempty + r, ((i >> 1) & 1) ^ 1, stop, a.status)) break;
     const int n = min(TC_TILES, a.tiles - mt * TC_TILES);
-    mbar_expect_tx(rawfull + r, (unsigned)(n * TC_CHUNK));
+    mbar_expect_tx(rawfull + r, (unsigned)(n * CH));
     for (int t = 0; t < n; t++)
-      bulk_g2s(raw + r * TC_RAW_BYTES + t * TC_CHUNK, a.w + ((size_t)(mt * TC_TILES + t) * a.nkb + kb) * TC_CHUNK, TC_CHUNK,
-               rawfull + r);
+      bulk_g2s(raw + r * RAW + t * CH, a.w + ((size_t)(mt * TC_TILES + t) * a.nkb + kb) * CH, CH, rawfull + r);
   }
   for (int j = max(0, i - 2); j < i; j++) tc_drain(rawfull + (j & 1), (j >> 1) & 1);
 }
 
+template <int T>
 __device__ void role_b(const TcArgs &a, uint8_t *stages, uint64_t *bfull, uint64_t *empty, volatile int *stop, int u0, int u1) {
   const int N = a.N;
   unsigned G = 0;
@@ -215,9 +232,9 @@ __device__ void role_b(const TcArgs &a, uint8_t *stages, uint64_t *bfull, uint64
     for (int g = 0; g < 4; g++, G++) {
       const int s = G % a.nstage;
       if (!tc_wait(empty + s, ((G / a.nstage) & 1) ^ 1, stop, a.status)) goto done;
-      const unsigned bytes = (unsigned)(N * 256 + (g == 3 ? N * 32 : 0));
+      const unsigned bytes = (unsigned)(N * 256 + (TcType<T>::MINS && g == 3 ? N * 32 : 0));
       mbar_expect_tx(bfull + s, bytes);
-      bulk_g2s(stages + (size_t)s * a.sbytes + TC_A_BYTES + TC_AMIN_BYTES, a.panel + (size_t)kb * panel_kb_bytes(N) + (size_t)g * N * 256,
+      bulk_g2s(stages + (size_t)s * a.sbytes + TC_A_BYTES + TcType<T>::A2, a.panel + (size_t)kb * panel_kb_bytes(N) + (size_t)g * N * 256,
                bytes, bfull + s);
     }
   }
@@ -225,8 +242,14 @@ done:
   for (unsigned j = G > (unsigned)a.nstage ? G - a.nstage : 0u; j < G; j++) tc_drain(bfull + j % a.nstage, (j / a.nstage) & 1);
 }
 
+template <int T>
 __device__ void role_dequant(const TcArgs &a, uint8_t *raw, uint8_t *stages, uint64_t *afull, uint64_t *empty, uint64_t *rawfull,
-                             uint64_t *rawempty, volatile int *stop, int u0, int u1, int warp, int lane) {
+                             uint64_t *rawempty, volatile int *stop, int u0, int u1, int warp, int lane);
+
+template <>
+__device__ void role_dequant<Q4_K>(const TcArgs &a, uint8_t *raw, uint8_t *stages, uint64_t *afull, uint64_t *empty, uint64_t *rawfull,
+                                   uint64_t *rawempty, volatile int *stop, int u0, int u1, int warp, int lane) {
+  constexpr int CH = TcType<Q4_K>::CHUNK, RAW = TC_TILES * CH;
   const int grp = lane >> 2, tig = lane & 3;
   unsigned G = 0;
   int i = 0;
@@ -235,7 +258,7 @@ __device__ void role_dequant(const TcArgs &a, uint8_t *raw, uint8_t *stages, uin
     bool ok = tc_wait(rawfull + r, (i >> 1) & 1, stop, a.status);
     if (!__all_sync(0xffffffffu, ok)) return;
     const bool present = mt * TC_TILES + warp < a.tiles;
-    const uint8_t *chunk = raw + r * TC_RAW_BYTES + warp * TC_CHUNK;
+    const uint8_t *chunk = raw + r * RAW + warp * CH;
     // scales of rows grp (rs 0) and grp + 8 (rs 1)
     Q4Scales S[2];
 #pragma unroll
@@ -287,6 +310,72 @@ __device__ void role_dequant(const TcArgs &a, uint8_t *raw, uint8_t *stages, uin
   }
 }
 
+// Q6_K: a weight is d*sc*(q - 32), sc an int8 per 16 columns, q 6 bits (low nibble
+// in ql, two high bits in qh). sc*(q - 32) reaches 4064 in magnitude, past the
+// integers f16 holds exactly, so A is written as two exact f16 terms with the
+// scale split into its even part and its last bit: A_hi = (sc & ~1)*(q - 32)
+// (even, <= 4096), A_lo = (sc & 1)*(q - 32); each term is one fma.rn.f16x2 from
+// the f16 value 64 + q (q placed in mantissa bits 4..9 of 64.0): (64 + q)*s - 96*s.
+template <>
+__device__ void role_dequant<Q6_K>(const TcArgs &a, uint8_t *raw, uint8_t *stages, uint64_t *afull, uint64_t *empty, uint64_t *rawfull,
+                                   uint64_t *rawempty, volatile int *stop, int u0, int u1, int warp, int lane) {
+  constexpr int CH = TcType<Q6_K>::CHUNK, RAW = TC_TILES * CH;
+  const int grp = lane >> 2, tig = lane & 3;
+  unsigned G = 0;
+  int i = 0;
+  for (int U = u0; U < u1; U++, i++) {
+    const int mt = U / a.nkb, r = i & 1;
+    bool ok = tc_wait(rawfull + r, (i >> 1) & 1, stop, a.status);
+    if (!__all_sync(0xffffffffu, ok)) return;
+    const bool present = mt * TC_TILES + warp < a.tiles;
+    const uint8_t *chunk = raw + r * RAW + warp * CH;
+    for (int g = 0; g < 4; g++, G++) {
+      const int s = G % a.nstage;
+      ok = tc_wait(empty + s, ((G / a.nstage) & 1) ^ 1, stop, a.status);
+      if (!__all_sync(0xffffffffu, ok)) return;
+      uint8_t *A = stages + (size_t)s * a.sbytes;
+      if (present) {
+        // stage g = columns 64g.. of the super-block: segment g >> 1, quarters 2hq, 2hq + 1
+        const int seg = g >> 1, hq = g & 1;
+        const uint4 l0 = *reinterpret_cast<const uint4 *>(chunk + (2 * seg) * 512 + lane * 16);
+        const uint4 l1 = *reinterpret_cast<const uint4 *>(chunk + (2 * seg + 1) * 512 + lane * 16);
+        const uint4 hv = *reinterpret_cast<const uint4 *>(chunk + 2048 + seg * 512 + lane * 16);
+        const uint32_t QL[2][4] = {{l0.x, l0.y, l0.z, l0.w}, {l1.x, l1.y, l1.z, l1.w}};
+        const uint32_t QH[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+        for (int wi = 0; wi < 4; wi++) {  // word order: (row grp, h 0), (row grp+8, h 0), (row grp, h 1), (row grp+8, h 1)
+          const int h = wi >> 1, rs = wi & 1, row = grp + 8 * rs;
+          uint8_t *dst = A + (2 * warp + rs) * 1024 + grp * 16 + (tig & 1) * 8;
+          const uint32_t u = prmt(QH[wi], 0x3120u);  // qh bytes c0 c2 c1 c3
+#pragma unroll
+          for (int qp = 0; qp < 2; qp++) {
+            const int quarter = 2 * hq + qp;
+            const uint32_t t = prmt(QL[qp][wi], 0x3120u);  // ql bytes b0 b2 b1 b3
+            // f16 64 + q of columns (4tig, 4tig+1) and (4tig+2, 4tig+3) of this 16-column run
+            const uint32_t n01 = (hq ? t : t << 4) & 0x00F000F0u, n23 = (hq ? t >> 8 : t >> 4) & 0x00F000F0u;
+            const uint32_t h01 = (u << (8 - 2 * quarter)) & 0x03000300u, h23 = (u >> (2 * quarter)) & 0x03000300u;
+            const uint32_t x01 = n01 | h01 | 0x54005400u, x23 = n23 | h23 | 0x54005400u;
+            const int sc = (int)(int8_t)chunk[3072 + 16 * row + seg * 8 + quarter * 2 + h];
+            const int se = sc & ~1, so = sc & 1;
+            const uint32_t she = __half_as_ushort(__int2half_rn(se)), nhe = __half_as_ushort(__int2half_rn(-96 * se));
+            const uint32_t sho = __half_as_ushort(__int2half_rn(so)), nho = __half_as_ushort(__int2half_rn(-96 * so));
+            const uint32_t se2 = she | (she << 16), ne2 = nhe | (nhe << 16), so2 = sho | (sho << 16), no2 = nho | (nho << 16);
+            const int kc = 4 * qp + 2 * h + (tig >> 1);  // core matrix along K of k = 32qp + 16h + 4tig
+            sts64(dst + kc * 128, hfma2(x01, se2, ne2), hfma2(x23, se2, ne2));
+            sts64(dst + TC_A_BYTES + kc * 128, hfma2(x01, so2, no2), hfma2(x23, so2, no2));
+          }
+        }
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(afull + s);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(rawempty + r);
+  }
+}
+
+template <int T>
 __device__ void role_mma(const TcArgs &a, uint32_t tbase, uint8_t *stages, uint64_t *bfull, uint64_t *afull, uint64_t *empty, uint64_t *accfull,
                          uint64_t *accempty, uint64_t *mnempty, uint64_t *drain, volatile int *stop, int u0, int u1) {
   const int N = a.N;
@@ -303,14 +392,19 @@ __device__ void role_mma(const TcArgs &a, uint32_t tbase, uint8_t *stages, uint6
       if (!tc_wait(bfull + s, (G / a.nstage) & 1, stop, a.status) || !tc_wait(afull + s, (G / a.nstage) & 1, stop, a.status))
         goto done;
       tc_fence_after();
-      const uint32_t sa = su32(stages + (size_t)s * a.sbytes), sb = sa + TC_A_BYTES + TC_AMIN_BYTES;
+      const uint32_t sa = su32(stages + (size_t)s * a.sbytes), sb = sa + TC_A_BYTES + TcType<T>::A2;
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         const uint64_t ad = sdesc(sa + k * 256, 128, 1024);
         mma_f16(tbase + b * N, ad, sdesc(sb + k * 256, 128, 1024), idesc, (g | k) != 0);
         mma_f16(tbase + b * N, ad, sdesc(sb + N * 128 + k * 256, 128, 1024), idesc, 1u);
+        if (!TcType<T>::MINS) {  // the low term of A (Q6_K) against both activation terms
+          const uint64_t al = sdesc(sa + TC_A_BYTES + k * 256, 128, 1024);
+          mma_f16(tbase + b * N, al, sdesc(sb + k * 256, 128, 1024), idesc, 1u);
+          mma_f16(tbase + b * N, al, sdesc(sb + N * 128 + k * 256, 128, 1024), idesc, 1u);
+        }
       }
-      if (g == 3) {
+      if (TcType<T>::MINS && g == 3) {
         if (!tc_wait(mnempty, (i & 1) ^ 1, stop, a.status)) goto done;
         tc_fence_after();
         mma_f16(tMn, sdesc(sa + TC_A_BYTES, 128, 256), sdesc(sb + N * 256, 128, 256), idesc, 0u);
@@ -375,7 +469,7 @@ __device__ __forceinline__ void out_cols16(const TcArgs &a, const uint32_t (&v)[
   }
 }
 
-template <int EPI>
+template <int T, int EPI>
 __device__ void role_epilogue(const TcArgs &a, uint32_t tbase, const float *cscale, uint64_t *accfull, uint64_t *accempty,
                               uint64_t *mnempty, volatile int *stop, int *pend, int u0, int u1, int q, int h, int lane) {
   const int N = a.N, m = 32 * q + lane;
@@ -390,50 +484,39 @@ __device__ void role_epilogue(const TcArgs &a, uint32_t tbase, const float *csca
     const int mt = P.mt, kb = P.kb, b = i & 1;
     const bool first = P.j == 0, last = P.j == P.len - 1, whole = P.len == a.nkb;
     const int row = mt * TC_M + m, tile = mt * TC_TILES + (m >> 4);
+    // super-block scales of the row: Q4_K d | dmin (chunk bytes 2048 + 16r), Q6_K d (3328 + 2r)
     uint32_t hdr = 0;
-    if (tile < a.tiles) hdr = ldg_u32(a.w + ((size_t)tile * a.nkb + kb) * TC_CHUNK + 2048 + 16 * (m & 15));
+    if (tile < a.tiles) {
+      const uint8_t *ck = a.w + ((size_t)tile * a.nkb + kb) * TcType<T>::CHUNK;
+      hdr = TcType<T>::MINS ? ldg_u32(ck + 2048 + 16 * (m & 15)) : ldg_u16(ck + 3328 + 2 * (m & 15));
+    }
     float brow = 0.f;
     if (last && whole && a.bias && row < a.rows) brow = __ldg(a.bias + row);
     bool ok = tc_wait(accfull + b, (i >> 1) & 1, stop, a.status);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    const float d = h2f(hdr), dmin = h2f(hdr >> 16);
+    const float d = h2f(hdr), dmin = TcType<T>::MINS ? h2f(hdr >> 16) : 0.f;
     const int slot = u0 >= mt * a.nkb ? 0 : 1;
     float *pdst = a.part + (size_t)(cta * 2 + slot) * N * TC_M + m;
     for (int c = cbeg; c < cend; c += 16) {
-      const bool two = false;  // (32 columns per round trip need more registers than this block has)
-      uint32_t r0[16], m0[16], y0[16], r1[16], m1[16], y1[16];
+      uint32_t r0[16], m0[16], y0[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++) r0[j] = m0[j] = y0[j] = 0u;
       if (ok) {
         tmem_ld16(lt + b * N + c, r0);
-        tmem_ld16(lt + 2 * N + c, m0);
+        if (TcType<T>::MINS) tmem_ld16(lt + 2 * N + c, m0);
         if (!first) tmem_ld16(lt + 3 * N + c, y0);
-        if (two) {
-          tmem_ld16(lt + b * N + c + 16, r1);
-          tmem_ld16(lt + 2 * N + c + 16, m1);
-          if (!first) tmem_ld16(lt + 3 * N + c + 16, y1);
-        }
         tmem_wait_ld();
         reg_fence(r0);
         reg_fence(m0);
         reg_fence(y0);
-        reg_fence(r1);
-        reg_fence(m1);
-        reg_fence(y1);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; j++) r0[j] = m0[j] = y0[j] = r1[j] = m1[j] = y1[j] = 0u;
       }
       epi_cols16(r0, m0, y0, first, d, dmin);
-      epi_cols16(r1, m1, y1, first, d, dmin);
       if (!last) {
-        if (ok) {
-          tmem_st16(lt + 3 * N + c, r0);
-          if (two) tmem_st16(lt + 3 * N + c + 16, r1);
-        }
+        if (ok) tmem_st16(lt + 3 * N + c, r0);
         continue;
       }
       out_cols16<EPI>(a, r0, cscale, c, whole, row, brow, lane, pdst);
-      if (two) out_cols16<EPI>(a, r1, cscale, c + 16, whole, row, brow, lane, pdst);
     }
     if (!last && ok) tmem_wait_st();
     tc_fence_before();
@@ -536,7 +619,7 @@ __device__ void finalize(const TcArgs &a, int mt, volatile int *stop) {
   }
 }
 
-template <int EPI>
+template <int T, int EPI>
 __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t *bfull = reinterpret_cast<uint64_t *>(smem), *afull = bfull + TC_MAXST, *empty = afull + TC_MAXST, *rawfull = empty + TC_MAXST,
@@ -548,7 +631,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs a) 
   int *pend = reinterpret_cast<int *>(smem + 392);  // M-tiles of this CTA's cut segments (first, last) or -1
   float *cscale = reinterpret_cast<float *>(smem + 512);  // N <= 128 floats
   uint8_t *raw = smem + TC_HDR;
-  uint8_t *stages = raw + 2 * TC_RAW_BYTES;
+  uint8_t *stages = raw + 2 * TC_TILES * TcType<T>::CHUNK;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, c = blockIdx.x;
   const int u0 = unit_start(a, c), u1 = unit_start(a, c + 1);
 
@@ -582,15 +665,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcArgs a) 
   const uint32_t tbase = *tslot;
 
   if (warp < TC_DQ) {
-    role_dequant(a, raw, stages, afull, empty, rawfull, rawempty, stop, u0, u1, warp, lane);
+    role_dequant<T>(a, raw, stages, afull, empty, rawfull, rawempty, stop, u0, u1, warp, lane);
   } else if (warp < TC_EPI0 + TC_EPIW) {
-    role_epilogue<EPI>(a, tbase, cscale, accfull, accempty, mnempty, stop, pend, u0, u1, warp & 3, 0, lane);
+    role_epilogue<T, EPI>(a, tbase, cscale, accfull, accempty, mnempty, stop, pend, u0, u1, warp & 3, 0, lane);
   } else if (warp == TC_RAWW) {
-    if (lane == 0) role_raw(a, raw, rawfull, rawempty, stop, u0, u1);
+    if (lane == 0) role_raw<T>(a, raw, rawfull, rawempty, stop, u0, u1);
   } else if (warp == TC_BW) {
-    if (lane == 0) role_b(a, stages, bfull, empty, stop, u0, u1);
+    if (lane == 0) role_b<T>(a, stages, bfull, empty, stop, u0, u1);
   } else if (warp == TC_MMAW) {
-    if (lane == 0) role_mma(a, tbase, stages, bfull, afull, empty, accfull, accempty, mnempty, drain, stop, u0, u1);
+    if (lane == 0) role_mma<T>(a, tbase, stages, bfull, afull, empty, accfull, accempty, mnempty, drain, stop, u0, u1);
   }
   __syncwarp();  // single-lane roles reconverge before the block barrier
   tc_fence_before();
@@ -710,7 +793,7 @@ __global__ void __launch_bounds__(256) gemm_tc_prep_kernel(const float *x, int l
 }  // namespace
 
 bool gemm_tc_supported(int type, int rows, int cols, int batch) {
-  return type == Q4_K && rows >= 1 && cols >= 256 && cols % 256 == 0 && batch >= 1 && batch <= GEMM_TC_MAX_BATCH;
+  return (type == Q4_K || type == Q6_K) && rows >= 1 && cols >= 256 && cols % 256 == 0 && batch >= 1 && batch <= GEMM_TC_MAX_BATCH;
 }
 size_t gemm_tc_panel_bytes(int batch, int cols) {
   const int N = (batch + 15) / 16 * 16;
@@ -723,7 +806,7 @@ size_t gemm_tc_part_floats(int batch, int sm_count) {
 int gemm_tc_mtiles(int rows) { return (rows + TC_M - 1) / TC_M; }
 
 cudaError_t launch_gemm_tc(const GemmTcLaunch &L, cudaStream_t s, int sm_count) {
-  if (!gemm_tc_supported(Q4_K, L.rows, L.cols, L.batch) || sm_count < 1) return cudaErrorInvalidValue;
+  if (!gemm_tc_supported(L.type, L.rows, L.cols, L.batch) || sm_count < 1) return cudaErrorInvalidValue;
   const int N = (L.batch + 15) / 16 * 16;
   gemm_tc_prep_kernel<<<N, 256, 0, s>>>(L.x, L.ldx, L.norm_w, L.eps, L.batch, N, L.cols, L.panel);
   cudaError_t e = cudaGetLastError();
@@ -745,8 +828,8 @@ cudaError_t launch_gemm_tc(const GemmTcLaunch &L, cudaStream_t s, int sm_count) 
   a.part = L.part;
   a.ctr = L.ctr;
   a.status = L.status;
-  a.sbytes = stage_bytes(N);
-  a.nstage = (int)((TC_SMEM_MAX - TC_HDR - 2 * TC_RAW_BYTES) / a.sbytes);
+  a.sbytes = stage_bytes(L.type, N);
+  a.nstage = (int)((TC_SMEM_MAX - TC_HDR - 2 * raw_bytes(L.type)) / a.sbytes);
   if (a.nstage > TC_MAXST) a.nstage = TC_MAXST;
   if (a.nstage < 2) return cudaErrorInvalidValue;
   uint32_t cols = 32;
@@ -757,24 +840,24 @@ cudaError_t launch_gemm_tc(const GemmTcLaunch &L, cudaStream_t s, int sm_count) 
   a.q = units / grid;
   a.rem = units % grid;
   a.thr = a.rem * (a.q + 1);
-  const size_t smem = (size_t)TC_HDR + 2 * TC_RAW_BYTES + (size_t)a.nstage * a.sbytes;
-  void (*kern)(const TcArgs) = nullptr;
-  switch (L.epi) {
-    case EPI_STORE: kern = gemm_tc_kernel<EPI_STORE>; break;
-    case EPI_ADD: kern = gemm_tc_kernel<EPI_ADD>; break;
-    case EPI_SILU: kern = gemm_tc_kernel<EPI_SILU>; break;
-    case EPI_GLU_SILU: kern = gemm_tc_kernel<EPI_GLU_SILU>; break;
-    case EPI_GLU_GELU: kern = gemm_tc_kernel<EPI_GLU_GELU>; break;
-    default: return cudaErrorInvalidValue;
-  }
-  static bool attr[5] = {false, false, false, false, false};
-  if (!attr[L.epi]) {
+  const size_t smem = (size_t)TC_HDR + 2 * raw_bytes(L.type) + (size_t)a.nstage * a.sbytes;
+  if (L.epi < 0 || L.epi > EPI_GLU_GELU) return cudaErrorInvalidValue;
+  using Kern = void (*)(const TcArgs);
+  static const Kern table[2][5] = {
+      {gemm_tc_kernel<Q4_K, EPI_STORE>, gemm_tc_kernel<Q4_K, EPI_ADD>, gemm_tc_kernel<Q4_K, EPI_SILU>,
+       gemm_tc_kernel<Q4_K, EPI_GLU_SILU>, gemm_tc_kernel<Q4_K, EPI_GLU_GELU>},
+      {gemm_tc_kernel<Q6_K, EPI_STORE>, gemm_tc_kernel<Q6_K, EPI_ADD>, gemm_tc_kernel<Q6_K, EPI_SILU>,
+       gemm_tc_kernel<Q6_K, EPI_GLU_SILU>, gemm_tc_kernel<Q6_K, EPI_GLU_GELU>}};
+  const int ti = L.type == Q4_K ? 0 : 1;
+  const Kern kern = table[ti][L.epi];
+  static bool attr[2][5] = {};
+  if (!attr[ti][L.epi]) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_MAX);
     if (e != cudaSuccess) return e;
     cudaFuncAttributes fa;
     if ((e = cudaFuncGetAttributes(&fa, kern)) != cudaSuccess) return e;
     if (fa.maxThreadsPerBlock < TC_THREADS) return cudaErrorLaunchOutOfResources;  // register budget of the build
-    attr[L.epi] = true;
+    attr[ti][L.epi] = true;
   }
   kern<<<grid, TC_THREADS, smem, s>>>(a);
   return cudaGetLastError();

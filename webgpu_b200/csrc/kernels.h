@@ -68,12 +68,13 @@ int gemv2_max_batch(int cols);
 
 // ------------------------------------------------ prompt-batch tensor-core GEMM
 // The same operation for a batch of activation rows on tcgen05 tensor cores
-// (Q4_K in the tile-16 layout; gemm_tc.cu). Scratch: `panel` holds the prepared
+// (Q4_K / Q6_K in the tile-16 layout; gemm_tc.cu). Scratch: `panel` holds the prepared
 // activations (gemm_tc_panel_bytes), `part` the partial sums of M-tiles cut
 // between CTAs (gemm_tc_part_floats), `ctr` gemm_tc_mtiles(rows) zeroed
 // counters (left zeroed). *status is set to 1 if a pipeline wait ran out.
 constexpr int GEMM_TC_MAX_BATCH = 128;
 struct GemmTcLaunch {
+  int type;  // Q4_K or Q6_K
   const uint8_t *w;
   int rows, cols;
   const float *x;

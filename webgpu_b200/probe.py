@@ -4,7 +4,7 @@
     python -m webgpu_b200.probe gemv ROWS COLS TYPE [LAUNCHES]   # wgd_op_gemv_tiled on random blocks
     python -m webgpu_b200.probe attention                        # wgd_op_attention, decode, L = 512/2048/4096
     python -m webgpu_b200.probe decode LAYERS STEPS [PERSISTENT]  # Llama-3-8B-width model, wgd_decode
-    python -m webgpu_b200.probe gemm ROWS COLS BATCH [LAUNCHES]  # wgd_op_gemm_tiled (Q4_K) vs the GEMV
+    python -m webgpu_b200.probe gemm ROWS COLS BATCH [LAUNCHES] [TYPE]  # wgd_op_gemm_tiled vs the GEMV (TYPE 12 Q4_K, 14 Q6_K)
     python -m webgpu_b200.probe prefill LAYERS BATCH [MIN_BATCH]  # Llama-3-8B-width prompt batches
 
 `gemv` repacks random GGUF blocks of TYPE (12 = Q4_K, 14 = Q6_K) into the tile layout once and calls the
@@ -92,35 +92,35 @@ def decode(layers: int, steps: int, persistent: int = 1) -> None:
     e.dispose()
 
 
-def gemm(rows: int, cols: int, batch: int, launches: int = 20) -> None:
-    """Times the tcgen05 GEMM and the tiled GEMV on one Q4_K matrix (CUDA events; the weights
-    of 8 copies rotate so that every launch reads them from HBM when they exceed L2)."""
+def gemm(rows: int, cols: int, batch: int, launches: int = 20, ttype: int = 12) -> None:
+    """Times the tcgen05 GEMM and the tiled GEMV on one Q4_K / Q6_K matrix (CUDA events; the
+    weights of 8 copies rotate so that every launch reads them from HBM when they exceed L2)."""
     import torch
     L = _native.lib()
-    nb = L.wgd_tiled_bytes(12, rows, cols)
+    nb = L.wgd_tiled_bytes(ttype, rows, cols)
     copies = max(1, min(8, (1 << 30) // nb))
-    raw = synth.random_blocks(12, rows * cols // 256, 2, 99)
+    raw = synth.random_blocks(ttype, rows * cols // 256, 2, 99)
     rd = torch.from_numpy(raw).cuda()
     mats = []
     for _ in range(copies):
         m = torch.empty(nb + 16, dtype=torch.uint8, device="cuda")
-        _native.check(L.wgd_op_repack_tiled(12, rows, cols, rd.data_ptr(), m.data_ptr(), None))
+        _native.check(L.wgd_op_repack_tiled(ttype, rows, cols, rd.data_ptr(), m.data_ptr(), None))
         mats.append(m)
     x = torch.randn(batch * cols, device="cuda")
     y = torch.empty(batch * rows, device="cuda")
     flops = 2.0 * rows * cols * batch
     for name, fn in (("gemm_tc", L.wgd_op_gemm_tiled), ("gemv_tiled", L.wgd_op_gemv_tiled)):
         for i in range(3):
-            _native.check(fn(12, rows, cols, mats[i % copies].data_ptr(), x.data_ptr(), batch, y.data_ptr(), None))
+            _native.check(fn(ttype, rows, cols, mats[i % copies].data_ptr(), x.data_ptr(), batch, y.data_ptr(), None))
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
         e0.record()
         for i in range(launches):
-            _native.check(fn(12, rows, cols, mats[i % copies].data_ptr(), x.data_ptr(), batch, y.data_ptr(), None))
+            _native.check(fn(ttype, rows, cols, mats[i % copies].data_ptr(), x.data_ptr(), batch, y.data_ptr(), None))
         e1.record()
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) / launches * 1000
-        print(f"{name} Q4_K {rows}x{cols} batch {batch}: {us:8.2f} us/launch  {flops / us / 1e6:8.1f} TFLOP/s "
+        print(f"{name} {'Q4_K' if ttype == 12 else 'Q6_K'} {rows}x{cols} batch {batch}: {us:8.2f} us/launch  {flops / us / 1e6:8.1f} TFLOP/s "
               f"(f16 MMA work x2: {2 * flops / us / 1e6:8.1f})  weights {nb / us / 1e3:7.1f} GB/s", flush=True)
     st = ctypes.c_int(0)
     _native.check(L.wgd_op_gemm_tiled_status(ctypes.byref(st)))
