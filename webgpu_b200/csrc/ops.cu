@@ -553,10 +553,12 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnArgs a
 // row's causal window as mask; the online softmax and the PV accumulation are
 // the decode kernel's, per vector. Splits of at least ATR_MIN_CHUNK keys are
 // merged by the CTA of the block that arrives last (same partial layout).
-constexpr int ATR_ROWS = 8, ATR_THREADS = 256, ATR_WARPS = 8, ATR_MIN_CHUNK = 512;
+constexpr int ATR_ROWS = 8, ATR_THREADS = 256, ATR_WARPS = 8, ATR_MIN_CHUNK = 128;
 
-template <int NI>
-__global__ void __launch_bounds__(ATR_THREADS, 1) attention_rows_kernel(const AttnArgs a) {
+// GM: the largest group size (query heads per kv head) the instance handles (4 or 8),
+// so that the per-vector registers of the smaller groups leave room for two CTAs per SM.
+template <int NI, int GM>
+__global__ void __launch_bounds__(ATR_THREADS, GM <= 4 ? 2 : 1) attention_rows_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) float sm[];
   const int G = a.heads / a.kv_heads, hd = a.hd, hd4 = hd >> 2, RS = hd + 4;
   const int QH = ATR_ROWS * G;
@@ -571,7 +573,7 @@ __global__ void __launch_bounds__(ATR_THREADS, 1) attention_rows_kernel(const At
   // the block's key range: from the first row's window start to the last row's position
   const int end_first = start + t0 + 1, kmin = end_first - (end_first < a.window ? end_first : a.window);
   const int kmax = start + t0 + nrows, L = kmax - kmin;
-  int chunk = (L + a.splits - 1) / a.splits;
+  int chunk = (L + (int)gridDim.y - 1) / (int)gridDim.y;  // gridDim.y <= a.splits (the partial stride)
   if (chunk < ATR_MIN_CHUNK) chunk = ATR_MIN_CHUNK;
   const int nsp = (L + chunk - 1) / chunk;
   if (sp >= nsp) return;
@@ -602,11 +604,11 @@ __global__ void __launch_bounds__(ATR_THREADS, 1) attention_rows_kernel(const At
 
   // this warp's vectors: qh = warp + 8i, i < G (row r = qh / G); row r's keys are
   // [P_r + 1 - min(P_r + 1, window), P_r] with P_r = start + t0 + r
-  float m[ATT_GMAX], l[ATT_GMAX];
-  float4 acc[ATT_GMAX][NI];
-  int lo[ATT_GMAX], hi[ATT_GMAX];
+  float m[GM], l[GM];
+  float4 acc[GM][NI];
+  int lo[GM], hi[GM];
 #pragma unroll
-  for (int i = 0; i < ATT_GMAX; i++) {
+  for (int i = 0; i < GM; i++) {
     m[i] = -FLT_MAX;
     l[i] = 0.f;
 #pragma unroll
@@ -623,16 +625,16 @@ __global__ void __launch_bounds__(ATR_THREADS, 1) attention_rows_kernel(const At
     __syncthreads();
     const float *ks = kv_s + (size_t)st * 2 * ATT_TILE * RS, *vs = ks + ATT_TILE * RS;
     const int key = tile + lane;
-    float sc[ATT_GMAX];
+    float sc[GM];
 #pragma unroll
-    for (int i = 0; i < ATT_GMAX; i++) sc[i] = 0.f;
+    for (int i = 0; i < GM; i++) sc[i] = 0.f;
     {
       const float4 *kr = reinterpret_cast<const float4 *>(ks + lane * RS);
 #pragma unroll 4
       for (int d4 = 0; d4 < hd4; d4++) {
         const float4 k4 = kr[d4];
 #pragma unroll
-        for (int i = 0; i < ATT_GMAX; i++) {
+        for (int i = 0; i < GM; i++) {
           if (i < G) {
             const float4 q = reinterpret_cast<const float4 *>(q_s + (warp + ATR_WARPS * i) * hd)[d4];
             sc[i] = fmaf(q.x, k4.x, fmaf(q.y, k4.y, fmaf(q.z, k4.z, fmaf(q.w, k4.w, sc[i]))));
@@ -640,9 +642,9 @@ __global__ void __launch_bounds__(ATR_THREADS, 1) attention_rows_kernel(const At
         }
       }
     }
-    float e[ATT_GMAX];
+    float e[GM];
 #pragma unroll
-    for (int i = 0; i < ATT_GMAX; i++) {
+    for (int i = 0; i < GM; i++) {
       e[i] = 0.f;
       if (i < G) {
         const bool live = lane < cnt && key >= lo[i] && key <= hi[i];
@@ -665,7 +667,7 @@ __global__ void __launch_bounds__(ATR_THREADS, 1) attention_rows_kernel(const At
         v[k] = d4 < hd4 ? vr[d4] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
-      for (int i = 0; i < ATT_GMAX; i++) {
+      for (int i = 0; i < GM; i++) {
         if (i < G) {
           const float w = __shfl_sync(0xffffffffu, e[i], j);
 #pragma unroll
@@ -680,7 +682,7 @@ __global__ void __launch_bounds__(ATR_THREADS, 1) attention_rows_kernel(const At
   const int PR = hd + 4;
   if (nsp == 1) {
 #pragma unroll
-    for (int i = 0; i < ATT_GMAX; i++) {
+    for (int i = 0; i < GM; i++) {
       const int qh = warp + ATR_WARPS * i, r = qh / G, g = qh - r * G;
       if (i >= G || r >= nrows) continue;
       float *o = a.out + ((int64_t)(t0 + r) * a.heads + kh * G + g) * hd;
@@ -696,7 +698,7 @@ __global__ void __launch_bounds__(ATR_THREADS, 1) attention_rows_kernel(const At
   }
   // partial rows: [(row * kv_heads + kh) * splits + sp][g] of acc | m | l | pad
 #pragma unroll
-  for (int i = 0; i < ATT_GMAX; i++) {
+  for (int i = 0; i < GM; i++) {
     const int qh = warp + ATR_WARPS * i, r = qh / G, g = qh - r * G;
     if (i >= G || r >= nrows) continue;
     float *part = a.part + (((int64_t)(t0 + r) * a.kv_heads + kh) * a.splits + sp) * G * PR + g * PR;
@@ -744,16 +746,18 @@ __global__ void __launch_bounds__(ATR_THREADS, 1) attention_rows_kernel(const At
   pdl_launch_dependents();
 }
 
-template <int NI>
+template <int NI, int GM>
 static cudaError_t launch_attention_rows_ni(const AttnArgs &a, size_t smem, cudaStream_t s, bool pdl) {
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attention_rows_kernel<NI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(attention_rows_kernel<NI, GM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     attr = true;
   }
   const int blocks = (a.n + ATR_ROWS - 1) / ATR_ROWS;
-  return launch_k(attention_rows_kernel<NI>, dim3(blocks * a.kv_heads, a.splits), dim3(ATR_THREADS), smem, s, pdl, a);
+  // no block reads more than capacity keys: splits beyond that many chunks would exit at once
+  const int ysplits = min(a.splits, (a.capacity + ATR_MIN_CHUNK - 1) / ATR_MIN_CHUNK);
+  return launch_k(attention_rows_kernel<NI, GM>, dim3(blocks * a.kv_heads, ysplits), dim3(ATR_THREADS), smem, s, pdl, a);
 }
 
 template <int NI>
@@ -775,8 +779,8 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
     return cudaErrorMisalignedAddress;
   if (a.n > 1 && !a.qkv && a.hd <= 256) {  // prompt batch: K/V tiles shared by ATR_ROWS query rows
     const size_t smem = sizeof(float) * ((size_t)ATR_ROWS * G * a.hd + 2 * 2 * ATT_TILE * (size_t)(a.hd + 4));
-    if (a.hd <= 128) return launch_attention_rows_ni<1>(a, smem, s, pdl);
-    return launch_attention_rows_ni<2>(a, smem, s, pdl);
+    if (a.hd <= 128) return G <= 4 ? launch_attention_rows_ni<1, 4>(a, smem, s, pdl) : launch_attention_rows_ni<1, 8>(a, smem, s, pdl);
+    return G <= 4 ? launch_attention_rows_ni<2, 4>(a, smem, s, pdl) : launch_attention_rows_ni<2, 8>(a, smem, s, pdl);
   }
   const int nst = a.hd <= 256 ? 2 : 1;
   const size_t smem = sizeof(float) * ((size_t)G * a.hd + 2 * (size_t)a.hd + (size_t)nst * 2 * ATT_TILE * (a.hd + 4));
