@@ -403,7 +403,7 @@ def main():
         pf_flops = projection_flops(c, len(prompt), world)
         pf_tflops = pf_flops / (pf_ms / 1000.0) / 1e12
         prefill = {"tokens": len(prompt), "batch": PREFILL_BATCH, "ms": pf_ms, "tok_per_s": len(prompt) / (pf_ms / 1000.0),
-                   "kernel": "gemm_tc_kernel (tcgen05.mma kind::f16 M128 N128, TMEM accumulators) for every Q4_K projection",
+                   "kernel": "gemm_tc_kernel (tcgen05.mma kind::f16 M128 N128, TMEM accumulators) for every Q4_K and Q6_K projection",
                    "projection_tflops": pf_tflops, "tensor_peak": tpk, "tensor_peak_kind": f"{tpk_kind} (bf16_tflops)",
                    "frac": pf_tflops / tpk,
                    "tensor_work_frac": 2 * pf_tflops / tpk,
