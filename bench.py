@@ -21,6 +21,9 @@ batches of 128 (untimed), then decode steps from position 512.
   prefill  the 512-token prompt prefilled again in batches of 128 (device
          time, max over ranks): every Q4_K projection runs on the tcgen05
          GEMM; projection TFLOP/s against the measured bf16 tensor peak.
+  sampled  the same decode with the reference's default draw (temperature 0.7,
+         topK 40, topP 0.9, seeded uniforms) on the device: wgd_decode_sample
+         (device time) and wgd_forward_sample per token (wall clock).
   cpu_baseline  the CPU restatement of the reference decoder (oracle/, float64)
          on a bounded sample of the same model, rank 0 only.
 
@@ -374,6 +377,36 @@ def main():
     clocks = clk.summary()
     tokens_dev = [int(buf[i]) for i in range(args.steps)]
 
+    # ---- sampled decode at the reference's default settings (temperature 0.7, topK 40, topP 0.9),
+    # drawn on the device: the device loop (wgd_decode_sample) and the per-token public call
+    # (wgd_forward_sample, token id in and out); the same seeded uniforms on every rank
+    T, K, P = 0.7, 40, 0.9
+    draws = np.random.default_rng(7).random(max(args.steps, args.warmup)).tolist()
+    us = (ctypes.c_double * len(draws))(*draws)
+    sbuf = (ctypes.c_int32 * len(draws))()
+    _native.check(L.wgd_decode_sample(eng.ctx, tok, start, args.warmup, T, K, P, us, sbuf), "decode_sample")
+    barrier()
+    _native.check(L.wgd_decode_sample(eng.ctx, tok, start, args.steps, T, K, P, us, sbuf), "decode_sample")
+    st = _native.StatsC()
+    L.wgd_stats_get(eng.ctx, ctypes.byref(st))
+    smp_ms = max_over_ranks(st.last_forward_ms)
+    it = iter(draws)
+    eng.random = lambda: next(it)
+    barrier()
+    t0 = time.perf_counter()
+    cur = tok
+    tokens_smp = []
+    for i in range(args.steps):
+        cur = eng.forward_sample([cur], start + i, T, K, P)
+        tokens_smp.append(cur)
+    barrier()
+    smp_e2e_s = max_over_ranks(time.perf_counter() - t0)
+    sampled = {"settings": {"temperature": T, "topK": K, "topP": P}, "tok_per_s": args.steps / (smp_ms / 1000.0),
+               "ms_per_step": smp_ms / args.steps, "e2e_tok_per_s": args.steps / smp_e2e_s,
+               "kernel": "sample_kernel (top-k by bitonic sort in shared memory, nucleus cut and draw in double) after "
+                         "each decode step; no logits readback",
+               "tokens_match_e2e": [int(sbuf[i]) for i in range(args.steps)] == tokens_smp}
+
     value = args.steps / (dev_ms / 1000.0)
     e2e = args.steps / e2e_s
     wbytes = weight_bytes(eng.gguf, c)
@@ -429,7 +462,7 @@ def main():
                        "l2": "weights (4.36 GB) exceed L2 every step", "rope": "adjacent-pair (llama GGUF rule)",
                        "layers": c.layers, "prefill_s": prefill_s},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 + 4, "d2h_bytes_per_step": 4},
-            "roofline": roof, "cpu_baseline": base, "clocks": clocks, "prefill": prefill,
+            "roofline": roof, "cpu_baseline": base, "clocks": clocks, "prefill": prefill, "sampled": sampled,
             "gpu_launches": launches,
             "tokens_match_e2e": tokens_dev == tokens_e2e,
         }

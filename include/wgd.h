@@ -142,6 +142,19 @@ WGD_API int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, int 
  * engine.ts:290-297, with sample() on the device). tokens_out receives the
  * `steps` generated ids (stopping early is the caller's business). */
 WGD_API int wgd_decode(wgd_ctx *ctx, int32_t first, int start, int steps, int32_t *tokens_out);
+/* One forward (as wgd_forward) and a draw from the last row's logits on the device, replacing the
+ * logits readback and sample() of PagedEngine.generate (engine.ts:291,305-324): top_k candidates by
+ * value (lower index first among equal values), p = exp((v - best) / temperature), the nucleus cut
+ * at top_p, draw = uniform * retained mass. `uniform` in [0, 1) takes the place of Math.random().
+ * Settings follow GenerationOptions (engine.ts:264): temperature in [0, 2] (0 = greedy), top_k
+ * 1..200, top_p in (0, 1]; otherwise WGD_EINVAL "Invalid sampling settings.". No finite logit:
+ * WGD_ENONFINITE. Under tensor parallelism every rank draws the same token (the logits are gathered). */
+WGD_API int wgd_forward_sample(wgd_ctx *ctx, const int32_t *ids, int n, int start, double temperature, int top_k, double top_p,
+                               double uniform, int32_t *token_out);
+/* wgd_decode with the same draw in place of the argmax: step i uses uniforms[i]; each drawn token
+ * is the next step's input without a host round trip. */
+WGD_API int wgd_decode_sample(wgd_ctx *ctx, int32_t first, int start, int steps, double temperature, int top_k, double top_p,
+                              const double *uniforms, int32_t *tokens_out);
 /* Kernels launched by the last forward (per token) or persistent call (1), for launch accounting. */
 WGD_API int wgd_kernels_per_token(wgd_ctx *ctx, int *count);
 /* KV cache bookkeeping for prefix reuse and reset (engine.ts:269-283,302). */
@@ -167,6 +180,10 @@ WGD_API int wgd_persistent_status(wgd_ctx *ctx, char *why, int why_len);
  * (a cudaStream_t, or NULL for the legacy default stream). They allocate
  * small per-device scratch (work counters) on first use. */
 
+/* The draw of wgd_forward_sample over n fp32 logits in device memory; the token is written to host
+ * memory (the call waits for it). */
+WGD_API int wgd_op_sample(const float *logits, int n, double temperature, int top_k, double top_p, double uniform,
+                          int32_t *token_out, void *stream);
 /* Bytes of one row in the device layout used by every weight kernel. */
 WGD_API int64_t wgd_dev_row_bytes(int ggml_type, int64_t cols);
 /* GGUF rows (raw bytes, row stride gguf row bytes) -> device layout rows. */

@@ -48,6 +48,8 @@ def lib():
         L.or_greedy.argtypes = [vp, i64]
         L.or_greedy_f64.restype = i64
         L.or_greedy_f64.argtypes = [vp, i64]
+        L.or_sample.restype = i64
+        L.or_sample.argtypes = [vp, i64, d, ctypes.c_int, d, d]
         L.or_set_threads.argtypes = [ctypes.c_int]
         L.or_rmsnorm.argtypes = [vp, vp, i64, i64, d, vp]
         L.or_rope.argtypes = [vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, d, d, d, ctypes.c_int,
@@ -105,6 +107,12 @@ def matmul(w: np.ndarray, ggml_type: int, rows: int, cols: int, x: np.ndarray, b
 def greedy(logits: np.ndarray) -> int:
     a = np.ascontiguousarray(logits, dtype=np.float32)
     return int(lib().or_greedy(_ptr(a), a.size))
+
+
+def sample(logits: np.ndarray, temperature: float, top_k: int, top_p: float, uniform: float) -> int:
+    """engine.ts:305-324 with Math.random() replaced by `uniform`; -1 when no logit is finite."""
+    a = np.ascontiguousarray(logits, dtype=np.float32)
+    return int(lib().or_sample(_ptr(a), a.size, float(temperature), int(top_k), float(top_p), float(uniform)))
 
 
 def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:

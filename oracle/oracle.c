@@ -11,6 +11,7 @@
  *   - fp32 dequant twin in WGSL order     src/core/shaders.ts:44-63 (weightFunction)
  *   - packed matmul expectation           src/verify.ts:32-35
  *   - greedy sample                       src/core/engine.ts:305-309
+ *   - temperature / top-k / top-p sample  src/core/engine.ts:310-323
  *   - RMSNorm / RoPE / attention fixtures src/verify.ts:39-66, src/verify-context.ts:8-41,
  *                                         src/core/shaders.ts:84-150,167-197
  *   - the float64 CPU decoder             scripts/verify-dense.mjs:138-211
@@ -246,6 +247,50 @@ int64_t or_greedy_f64(const double *logits, int64_t n) {
   double best = -INFINITY; int64_t id = -1;
   for (int64_t i = 0; i < n; i++) if (isfinite(logits[i]) && logits[i] > best) { best = logits[i]; id = i; }
   return id;
+}
+
+/* engine.ts:305-324 (temperature > 0), step for step: a candidate list kept sorted by
+ * value (a new value goes after the equal ones, as JS's stable sort leaves it), a
+ * finite logit enters while the list is short or when it beats the last entry, the
+ * entry past top_k is dropped; probability exp((v - best) / temperature) in double;
+ * total and the nucleus mass summed in list order; draw = uniform * retained,
+ * subtracted in list order. `uniform` stands for Math.random(). Returns -1 when no
+ * logit is finite (the reference throws). temperature == 0 is or_greedy. */
+int64_t or_sample(const float *logits, int64_t n, double temperature, int top_k, double top_p, double uniform) {
+  const int64_t best_id = or_greedy(logits, n);
+  if (best_id < 0) return -1;
+  if (temperature == 0) return best_id;
+  const double best = logits[best_id];
+  int64_t *id = malloc(sizeof(int64_t) * (size_t)(top_k + 1));
+  double *val = malloc(sizeof(double) * (size_t)(top_k + 1)), *prob = malloc(sizeof(double) * (size_t)(top_k + 1));
+  int count = 0;
+  for (int64_t i = 0; i < n; i++) {
+    if (!isfinite(logits[i])) continue;
+    const double v = logits[i];
+    if (count < top_k || v > val[count - 1]) {
+      int at = count;
+      while (at > 0 && val[at - 1] < v) at--;
+      for (int j = count; j > at; j--) { id[j] = id[j - 1]; val[j] = val[j - 1]; prob[j] = prob[j - 1]; }
+      id[at] = i; val[at] = v; prob[at] = exp((v - best) / temperature);
+      if (++count > top_k) count--;
+    }
+  }
+  double total = 0;
+  for (int j = 0; j < count; j++) total += prob[j];
+  double retained = 0;
+  int cutoff = 0;
+  for (; cutoff < count; cutoff++) {
+    retained += prob[cutoff];
+    if (retained / total >= top_p) { cutoff++; break; }
+  }
+  double draw = uniform * retained;
+  int64_t out = best_id;
+  for (int j = 0; j < cutoff; j++) {
+    draw -= prob[j];
+    if (draw <= 0) { out = id[j]; break; }
+  }
+  free(id); free(val); free(prob);
+  return out;
 }
 
 /* ------------------------------------------------------- primitive references */

@@ -62,6 +62,12 @@ SIGNATURES = {
     "wgd_model_placement": (c_int, [c_void_p, ctypes.POINTER(c_uint64), ctypes.POINTER(c_uint64)]),
     "wgd_forward": (c_int, [c_void_p, ctypes.POINTER(c_int32), c_int, c_int, c_int, ctypes.POINTER(c_int32), ctypes.POINTER(c_float)]),
     "wgd_decode": (c_int, [c_void_p, c_int32, c_int, c_int, ctypes.POINTER(c_int32)]),
+    "wgd_forward_sample": (c_int, [c_void_p, ctypes.POINTER(c_int32), c_int, c_int, ctypes.c_double, c_int, ctypes.c_double,
+                                   ctypes.c_double, ctypes.POINTER(c_int32)]),
+    "wgd_decode_sample": (c_int, [c_void_p, c_int32, c_int, c_int, ctypes.c_double, c_int, ctypes.c_double,
+                                  ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_int32)]),
+    "wgd_op_sample": (c_int, [c_void_p, c_int, ctypes.c_double, c_int, ctypes.c_double, ctypes.c_double, ctypes.POINTER(c_int32),
+                              c_void_p]),
     "wgd_kernels_per_token": (c_int, [c_void_p, ctypes.POINTER(c_int)]),
     "wgd_truncate_kv": (c_int, [c_void_p, c_int]),
     "wgd_cancel": (None, [c_void_p]),

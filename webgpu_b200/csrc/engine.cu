@@ -145,14 +145,20 @@ struct wgd_ctx {
   float *tc_part = nullptr;
   unsigned *tc_ctr = nullptr;
   int *tc_status = nullptr;  // device address of h_io[IO_TC]
+  // device sampling (sample.cu): settings, per-step uniforms [context], CTA keys, counter
+  SampleParams *d_sparams = nullptr;
+  double *d_uniform = nullptr;
+  uint64_t *smp_part = nullptr;
+  unsigned *smp_ctr = nullptr;
+  int *d_ptok = nullptr;  // token slot of the persistent kernel when the draw replaces its argmax
   int32_t *h_io = nullptr;  // pinned: [0] start, [1] argmax, [2..] ids
   // graph
   bool graphs = true;
-  cudaGraphExec_t decode_exec = nullptr, chain_exec = nullptr;
-  cudaGraph_t decode_graph = nullptr, chain_graph = nullptr;
+  cudaGraphExec_t decode_exec = nullptr, chain_exec = nullptr, chain_smp_exec = nullptr;
+  cudaGraph_t decode_graph = nullptr, chain_graph = nullptr, chain_smp_graph = nullptr;
   int *d_tokens = nullptr, *d_step = nullptr;
   int kernels = 0;  // kernels launched by the last enqueued forward
-  int decode_kernels = 0, chain_kernels = 0;  // kernels in the captured graphs
+  int decode_kernels = 0, chain_kernels = 0, chain_smp_kernels = 0;  // kernels in the captured graphs
   std::atomic<int> cancel{0};
   wgd_stats st{};
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -211,8 +217,10 @@ static void free_all(wgd_ctx *ctx) {
   if (ctx->decode_graph) cudaGraphDestroy(ctx->decode_graph);
   if (ctx->chain_exec) cudaGraphExecDestroy(ctx->chain_exec);
   if (ctx->chain_graph) cudaGraphDestroy(ctx->chain_graph);
-  ctx->decode_exec = ctx->chain_exec = nullptr;
-  ctx->decode_graph = ctx->chain_graph = nullptr;
+  if (ctx->chain_smp_exec) cudaGraphExecDestroy(ctx->chain_smp_exec);
+  if (ctx->chain_smp_graph) cudaGraphDestroy(ctx->chain_smp_graph);
+  ctx->decode_exec = ctx->chain_exec = ctx->chain_smp_exec = nullptr;
+  ctx->decode_graph = ctx->chain_graph = ctx->chain_smp_graph = nullptr;
   for (auto &a : ctx->allocs) cudaFree(a.p);
   ctx->allocs.clear();
   ctx->allocated = 0;
@@ -799,6 +807,11 @@ extern "C" int wgd_model_end(wgd_ctx *ctx) {
   if ((rc = ctx_alloc_t(ctx, &ctx->gemv_ctr, 2 * 1024, "gemv counters"))) return rc;
   if ((rc = ctx_alloc_t(ctx, &ctx->am_part, 2 * 256, "argmax partials")) || (rc = ctx_alloc_t(ctx, &ctx->am_ctr, 4, "argmax counter")))
     return rc;
+  if ((rc = ctx_alloc_t(ctx, &ctx->d_sparams, 1, "sampling settings")) ||
+      (rc = ctx_alloc_t(ctx, &ctx->d_uniform, (size_t)ctx->context, "sampling draws")) ||
+      (rc = ctx_alloc_t(ctx, &ctx->smp_part, (size_t)SAMPLE_MAX_GRID * SAMPLE_MAX_K, "sampling candidates")) ||
+      (rc = ctx_alloc_t(ctx, &ctx->smp_ctr, 4, "sampling counter")) || (rc = ctx_alloc_t(ctx, &ctx->d_ptok, 4, "decode token slot")))
+    return rc;
   ctx->staging_bytes = 64u << 20;
   if ((rc = ctx_alloc_t(ctx, &ctx->staging, ctx->staging_bytes, "upload staging"))) return rc;
   // RoPE (cos, sin) tables, one per distinct (theta, scale): angle = pos * scale / theta^(2i/rot),
@@ -1204,7 +1217,52 @@ static int enqueue_forward(wgd_ctx *ctx, int n, bool want_logits_rows, bool io =
   return WGD_OK;
 }
 
+// Draw of sample.cu over ctx->logits (whole vocabulary) into d_argmax, with the
+// settings in d_sparams and the uniform d_uniform[step ? *step : 0].
+static int enqueue_sample(wgd_ctx *ctx, const int *step) {
+  SampleArgs s{};
+  s.logits = ctx->logits;
+  s.n = ctx->c.vocab;
+  s.params = ctx->d_sparams;
+  s.uniform = ctx->d_uniform;
+  s.step = step;
+  s.out = ctx->d_argmax;
+  s.part = ctx->smp_part;
+  s.ctr = ctx->smp_ctr;
+  CK(launch_sample(s, ctx->sm_count, ctx->stream, true));
+  ctx->kernels += 1;
+  return WGD_OK;
+}
+
+// GenerationOptions rules of PagedEngine.generate (engine.ts:263-264).
+static bool sampling_ok(double temperature, int top_k, double top_p) {
+  return std::isfinite(temperature) && temperature >= 0 && temperature <= 2 && top_k >= 1 && top_k <= SAMPLE_MAX_K &&
+         std::isfinite(top_p) && top_p > 0 && top_p <= 1;
+}
+
+static int forward_impl(wgd_ctx *ctx, const int32_t *ids, int n, int start, int want, int32_t *argmax_out, float *logits_out,
+                        bool sampled);
+
 extern "C" int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, int want, int32_t *argmax_out, float *logits_out) {
+  return forward_impl(ctx, ids, n, start, want, argmax_out, logits_out, false);
+}
+
+extern "C" int wgd_forward_sample(wgd_ctx *ctx, const int32_t *ids, int n, int start, double temperature, int top_k, double top_p,
+                                  double uniform, int32_t *token_out) {
+  if (!ctx || !ids || !token_out) return fail(WGD_EINVAL, "null argument");
+  if (!sampling_ok(temperature, top_k, top_p)) return fail(WGD_EINVAL, "Invalid sampling settings.");
+  if (!(uniform >= 0 && uniform < 1)) return fail(WGD_EINVAL, "the uniform draw must lie in [0, 1)");
+  if (temperature == 0) return forward_impl(ctx, ids, n, start, 1, token_out, nullptr, false);
+  if (!ctx->ended) return fail(WGD_ESTATE, "Load a model first.");
+  CK(cudaSetDevice(ctx->device));
+  const SampleParams sp{temperature, top_p, top_k, 0};
+  CK(cudaMemcpyAsync(ctx->d_sparams, &sp, sizeof(sp), cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaMemcpyAsync(ctx->d_uniform, &uniform, sizeof(double), cudaMemcpyHostToDevice, ctx->stream));
+  return forward_impl(ctx, ids, n, start, 1, token_out, nullptr, true);
+}
+
+static int forward_impl(wgd_ctx *ctx, const int32_t *ids, int n, int start, int want, int32_t *argmax_out, float *logits_out,
+                        bool sampled) {
   if (!ctx || !ids) return fail(WGD_EINVAL, "null argument");
   if (!ctx->ended) return fail(WGD_ESTATE, "Load a model first.");
   std::string missing;
@@ -1221,7 +1279,7 @@ extern "C" int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, i
   memcpy(ctx->h_io + 2, ids, sizeof(int32_t) * n);
   CK(cudaEventRecord(ctx->ev0, ctx->stream));
   int rc;
-  const bool gather_logits = want == 2;
+  const bool gather_logits = want == 2 || (sampled && ctx->tp_size > 1);  // the draw reads the whole row on every rank
   const bool persist = n == 1 && ctx->persist_ok && ctx->persist_on;
   if (persist) {
     ctx->h_io[IO_CANCEL] = 0;
@@ -1245,6 +1303,12 @@ extern "C" int wgd_forward(wgd_ctx *ctx, const int32_t *ids, int n, int start, i
   } else {
     if ((rc = enqueue_forward(ctx, n, gather_logits))) return rc;
     ctx->st.kernel_launches += ctx->kernels;
+  }
+  if (sampled) {
+    const int before = ctx->kernels;
+    if ((rc = enqueue_sample(ctx, nullptr))) return rc;
+    ctx->st.kernel_launches += ctx->kernels - before;
+    CK(cudaMemcpyAsync(ctx->h_io + 1, ctx->d_argmax, sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream));
   }
   CK(cudaEventRecord(ctx->ev1, ctx->stream));
   if (want == 2 && logits_out) {
@@ -1343,6 +1407,103 @@ extern "C" int wgd_decode(wgd_ctx *ctx, int32_t first, int start, int steps, int
   ctx->st.forwards += steps;
   ctx->st.tokens += steps;
   if (ctx->tp && tp_failed(ctx->tp)) return fail(WGD_ETIMEOUT, "a tensor-parallel peer did not answer within the wait limit");
+  if (err == 2) return fail(WGD_ENONFINITE, "Inference produced non-finite logits. Stop and report this model/runtime combination.");
+  return WGD_OK;
+}
+
+// wgd_decode with the draw of sample.cu in place of the argmax. The persistent kernel (when
+// eligible) runs one token per launch, reading its input token and position from device
+// memory; the draw and the advance step follow it on the stream, so there is no host round
+// trip between tokens. Otherwise the per-kernel step, the draw and the advance step are
+// captured once into a graph (settings and draws are device data, so it serves any of them).
+extern "C" int wgd_decode_sample(wgd_ctx *ctx, int32_t first, int start, int steps, double temperature, int top_k, double top_p,
+                                 const double *uniforms, int32_t *tokens_out) {
+  if (!ctx || !tokens_out || !uniforms) return fail(WGD_EINVAL, "null argument");
+  if (!sampling_ok(temperature, top_k, top_p)) return fail(WGD_EINVAL, "Invalid sampling settings.");
+  if (temperature == 0) return wgd_decode(ctx, first, start, steps, tokens_out);
+  if (!ctx->ended) return fail(WGD_ESTATE, "Load a model first.");
+  std::string missing;
+  if (!all_uploaded(ctx, &missing)) return fail(WGD_ESTATE, "weights not uploaded: " + missing);
+  if (steps < 1 || start < 0 || start + steps > ctx->context) return fail(WGD_EINVAL, "positions exceed the context length");
+  if (first < 0 || first >= ctx->c.vocab) return fail(WGD_EINVAL, "token id out of range");
+  for (int i = 0; i < steps; i++)
+    if (!(uniforms[i] >= 0 && uniforms[i] < 1)) return fail(WGD_EINVAL, "the uniform draws must lie in [0, 1)");
+  if (ctx->cancel.exchange(0)) return fail(WGD_ECANCELLED, "Stopped by user");
+  CK(cudaSetDevice(ctx->device));
+  int rc;
+  const SampleParams sp{temperature, top_p, top_k, 0};
+  CK(cudaMemcpyAsync(ctx->d_sparams, &sp, sizeof(sp), cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaMemcpyAsync(ctx->d_uniform, uniforms, sizeof(double) * steps, cudaMemcpyHostToDevice, ctx->stream));
+  ctx->h_io[0] = start;
+  ctx->h_io[2] = first;
+  ctx->h_io[3] = 0;
+  CK(cudaMemcpyAsync(ctx->d_start, ctx->h_io, sizeof(int32_t), cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaMemcpyAsync(ctx->d_ids, ctx->h_io + 2, sizeof(int32_t), cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaMemcpyAsync(ctx->d_step, ctx->h_io + 3, sizeof(int32_t), cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaMemsetAsync(ctx->d_err, 0, sizeof(int32_t), ctx->stream));
+  const bool persist = ctx->persist_ok && ctx->persist_on;
+  if (!persist && !ctx->chain_smp_exec && !ctx->paging) {
+    CK(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+    rc = enqueue_forward(ctx, 1, ctx->tp_size > 1, false);
+    if (!rc) rc = enqueue_sample(ctx, ctx->d_step);
+    if (!rc) {
+      cudaError_t e = launch_advance(ctx->d_ids, ctx->d_start, ctx->d_argmax, ctx->d_tokens, ctx->d_step, ctx->d_err, ctx->stream, true);
+      if (e != cudaSuccess) rc = fail(WGD_ECUDA, std::string("advance: ") + cudaGetErrorString(e));
+      ctx->kernels += 1;
+    }
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+    if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+    if (e != cudaSuccess) return fail(WGD_ECUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    ctx->chain_smp_graph = g;
+    CK(cudaGraphInstantiate(&ctx->chain_smp_exec, g, 0));
+    ctx->chain_smp_kernels = ctx->kernels;
+  }
+  PersistArgs pa = ctx->pargs;
+  if (persist) {
+    ctx->h_io[IO_CANCEL] = 0;
+    pa.dev_first = ctx->d_ids;
+    pa.dev_start = ctx->d_start;
+    pa.steps = 1;
+    pa.tokens = ctx->d_ptok;
+    CK(cudaMemsetAsync(pa.status, 0, 4 * sizeof(int), ctx->stream));
+  }
+  ctx->st.streamed_bytes = 0;
+  CK(cudaEventRecord(ctx->ev0, ctx->stream));
+  for (int i = 0; i < steps; i++) {
+    if (persist) {
+      CK(cudaMemsetAsync(pa.bar, 0, sizeof(unsigned), ctx->stream));  // arrivals only
+      CK(launch_persist(pa, ctx->sm_count, ctx->stream));
+      ctx->kernels = 1;
+      if ((rc = enqueue_sample(ctx, ctx->d_step))) return rc;
+      CK(launch_advance(ctx->d_ids, ctx->d_start, ctx->d_argmax, ctx->d_tokens, ctx->d_step, ctx->d_err, ctx->stream, true));
+      ctx->kernels += 1;
+      ctx->st.kernel_launches += ctx->kernels;
+    } else if (ctx->paging) {
+      if ((rc = enqueue_forward(ctx, 1, ctx->tp_size > 1, false))) return rc;
+      if ((rc = enqueue_sample(ctx, ctx->d_step))) return rc;
+      CK(launch_advance(ctx->d_ids, ctx->d_start, ctx->d_argmax, ctx->d_tokens, ctx->d_step, ctx->d_err, ctx->stream, true));
+      ctx->kernels += 1;
+      ctx->st.kernel_launches += ctx->kernels;
+    } else {
+      CK(cudaGraphLaunch(ctx->chain_smp_exec, ctx->stream));
+      ctx->kernels = ctx->chain_smp_kernels;
+      ctx->st.kernel_launches += ctx->kernels;
+    }
+  }
+  CK(cudaEventRecord(ctx->ev1, ctx->stream));
+  if (persist) CK(cudaMemcpyAsync(ctx->h_io + IO_STATUS, pa.status, 4 * sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+  CK(cudaMemcpyAsync(tokens_out, ctx->d_tokens, sizeof(int32_t) * steps, cudaMemcpyDeviceToHost, ctx->stream));
+  int32_t err = 0;
+  CK(cudaMemcpyAsync(&err, ctx->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream));
+  CK(cudaStreamSynchronize(ctx->stream));
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, ctx->ev0, ctx->ev1);
+  ctx->st.last_forward_ms = ms;
+  ctx->st.forwards += steps;
+  ctx->st.tokens += steps;
+  if (ctx->tp && tp_failed(ctx->tp)) return fail(WGD_ETIMEOUT, "a tensor-parallel peer did not answer within the wait limit");
+  if (persist && (rc = persist_status(ctx))) return rc;
   if (err == 2) return fail(WGD_ENONFINITE, "Inference produced non-finite logits. Stop and report this model/runtime combination.");
   return WGD_OK;
 }

@@ -175,6 +175,29 @@ cudaError_t launch_argmax(const float *x, int n, int *out_idx, float *out_val, f
                           bool pdl);
 int argmax_blocks(int n);
 
+// Temperature / top-k / top-p draw over one row of logits (sample.cu). Settings and
+// the uniform draws live in device memory so that a captured graph serves any of them.
+constexpr int SAMPLE_MAX_K = 200;     // the reference's largest topK
+constexpr int SAMPLE_MAX_GRID = 256;  // CTAs of one launch (part holds GRID * top_k keys)
+struct SampleParams {
+  double temperature;  // > 0 draws, == 0 greedy
+  double top_p;        // nucleus mass in (0, 1]
+  int top_k;           // 1..SAMPLE_MAX_K
+  int pad;
+};
+struct SampleArgs {
+  const float *logits;
+  int n;
+  const SampleParams *params;
+  const double *uniform;  // uniform[step ? *step : 0], in [0, 1)
+  const int *step;
+  int *out;               // token; -1 when no logit is finite
+  uint64_t *part;         // SAMPLE_MAX_GRID * SAMPLE_MAX_K keys
+  unsigned *ctr;          // one zeroed counter (left zeroed)
+};
+cudaError_t launch_sample(const SampleArgs &a, int sm_count, cudaStream_t s, bool pdl);
+int sample_grid(int n, int sm_count);
+
 // Device decode loop step: ids[0] = *argmax; *start += 1; tokens[*step] = *argmax; ++*step.
 // A non-finite row (argmax -1) sets *err and feeds token 0.
 cudaError_t launch_advance(int *ids, int *start, const int *argmax, int *tokens, int *step, int *err, cudaStream_t s, bool pdl);

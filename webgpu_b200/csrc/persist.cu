@@ -925,10 +925,11 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
   unsigned gen = 0;
   if (tid == 0) gen = ld_acquire(a.bar + 1);
   unsigned g = 0;  // ring stage counter, in step with the producer
-  int token = a.first;
+  int token = a.dev_first ? __ldcg(a.dev_first) : a.first;
+  const int start = a.dev_start ? __ldcg(a.dev_start) : a.start;
   bool att_staged = false;  // attention stage 0 was filled during the previous phase
   for (int step = 0; step < a.steps; step++) {
-    const int pos = a.start + step;
+    const int pos = start + step;
     // embedding row of the token (engine.ts:140-145), spread over the CTAs
     if (comp) {
       const int per = (a.hidden + grid - 1) / grid;

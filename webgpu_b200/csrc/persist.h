@@ -59,6 +59,7 @@ struct PersistArgs {
   float *x;  // hidden state [hidden]
   // tokens
   int first, start, steps;
+  const int *dev_first, *dev_start;  // non-null: first token and position read from device memory
   int *tokens;          // [steps] greedy tokens
   const int *cancel;    // host-mapped flag polled between tokens, or null
   // scratch

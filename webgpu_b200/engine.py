@@ -114,34 +114,20 @@ class ByteTokenizer:
         return out.decode("utf-8", errors="replace")
 
 
-def sample(logits: np.ndarray, temperature: float, top_k: int, top_p: float, rng=random) -> int:
-    """engine.ts:305-324."""
-    x = np.asarray(logits, dtype=np.float64)
-    finite = np.isfinite(x)
-    if not finite.any():
-        raise ValueError("Inference produced non-finite logits. Stop and report this model/runtime combination.")
-    masked = np.where(finite, x, -np.inf)
-    best_id = int(np.argmax(masked))
-    best = masked[best_id]
-    if temperature == 0:
-        return best_id
-    order = np.argsort(-masked, kind="stable")
-    cand = [int(i) for i in order[:top_k] if finite[i]]
-    probs = [math.exp((x[i] - best) / temperature) for i in cand]
-    total = sum(probs)
-    retained, cutoff = 0.0, 0
-    while cutoff < len(cand):
-        retained += probs[cutoff]
-        if retained / total >= top_p:
-            cutoff += 1
-            break
-        cutoff += 1
-    draw = rng.random() * retained
-    for i in range(cutoff):
-        draw -= probs[i]
-        if draw <= 0:
-            return cand[i]
-    return best_id
+def sample(logits, temperature: float, top_k: int, top_p: float, rng=random.random) -> int:
+    """engine.ts:305-324 for a host row of logits, drawn on the device (wgd_op_sample) with one
+    uniform number from `rng` (Math.random()). Raises the reference's error when no logit is
+    finite. The engine itself never reads logits back: generate draws with wgd_forward_sample."""
+    import torch
+
+    x = torch.as_tensor(np.ascontiguousarray(logits, dtype=np.float32)).cuda()
+    tok = ctypes.c_int32(-1)
+    st = _native.lib().wgd_op_sample(x.data_ptr(), x.numel(), float(temperature), int(top_k), float(top_p), rng(),
+                                     ctypes.byref(tok), None)
+    if st == _native.WGD_ENONFINITE:
+        raise ValueError(_native.last_error())
+    _native.check(st, "sample")
+    return tok.value
 
 
 class PagedEngine:
@@ -164,6 +150,7 @@ class PagedEngine:
         self.rank = 0
         self.device = 0
         self._logits = None
+        self.random = random.random  # the uniform draw per sampled token (Math.random())
 
     # ------------------------------------------------------------------ load
     def load(self, src, options: dict | None = None, signal=None) -> ModelInfo:
@@ -327,6 +314,23 @@ class PagedEngine:
             return None
         return (out.value, self._logits.copy()) if want == 2 else out.value
 
+    def forward_sample(self, ids, start: int, temperature: float, top_k: int, top_p: float) -> int:
+        """engine.ts:138-180 and sample() (engine.ts:305-324) in one device call: the token is
+        drawn on the device from the last row's logits with one uniform number from
+        self.random (Math.random()); only the token id comes back."""
+        L = _native.lib()
+        n = len(ids)
+        arr = (ctypes.c_int32 * n)(*ids)
+        out = ctypes.c_int32(-1)
+        st = L.wgd_forward_sample(self.ctx, arr, n, start, float(temperature), int(top_k), float(top_p), self.random(),
+                                  ctypes.byref(out))
+        if st == _native.WGD_ECANCELLED:
+            raise AbortError("Stopped by user")
+        if st == _native.WGD_ENONFINITE:
+            raise ValueError(_native.last_error())
+        _native.check(st, "forward_sample")
+        return out.value
+
     # --------------------------------------------------------------- generate
     def generate(self, messages, options: dict | None = None, signal=None):
         """engine.ts:257-301."""
@@ -380,14 +384,17 @@ class PagedEngine:
                     raise AbortError("Stopped by user")
                 batch = prompt[i:i + self.batch]
                 last = i + len(batch) == len(prompt)
-                result = self.forward(batch, i, last, want_logits=last and not greedy)
+                if last and not greedy:
+                    result = self.forward_sample(batch, i, temperature, top_k, top_p)
+                else:
+                    result = self.forward(batch, i, last)
                 self.tokens_in_cache += batch
             generated: list[int] = []
             text = ""
             for i in range(limit):
                 if signal is not None and signal.is_set():
                     raise AbortError("Stopped by user")
-                token = result if greedy else sample(result[1], temperature, top_k, top_p)
+                token = result
                 if token in self.tokenizer.eos:
                     break
                 generated.append(token)
@@ -397,7 +404,9 @@ class PagedEngine:
                 yield TokenEvent(token, text, delta, len(generated), len(prompt), self.context,
                                  time.perf_counter() - started, self.stats())
                 if i + 1 < limit:
-                    result = self.forward([token], len(self.tokens_in_cache), True, want_logits=not greedy)
+                    pos = len(self.tokens_in_cache)
+                    result = (self.forward([token], pos, True) if greedy else
+                              self.forward_sample([token], pos, temperature, top_k, top_p))
                     self.tokens_in_cache.append(token)
         except BaseException:
             self.tokens_in_cache = []
