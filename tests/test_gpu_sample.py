@@ -187,7 +187,7 @@ def test_generate_samples_on_device(cuda):
     """PagedEngine.generate with the default settings (temperature 0.7, topK 40, topP 0.9): the
     streamed tokens equal host draws over the device logits with the same uniforms."""
     spec = synth.tiny_dense("llama")
-    e = _engine(spec, 256, 16)
+    e = _engine(spec, 256, 32)  # the whole prompt in one batch, as the replay runs it
     uniforms = [0.11, 0.93, 0.42, 0.67, 0.05, 0.5]
     it = iter(uniforms)
     e.random = lambda: next(it)
