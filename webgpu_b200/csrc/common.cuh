@@ -78,6 +78,22 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Base-254 digits of t in [-127, 127]: a = rint(t), b = rint((t - a) * 254),
+// c = rint(((t - a) * 254 - b) * 254), each as a two's-complement byte in the low 8 bits.
+// Rounding to the nearest integer (ties to even) of |x| < 2^22 is (x + 1.5*2^23) - 1.5*2^23,
+// and the integer sits in the low mantissa bits of x + 1.5*2^23: additions only, no
+// float->int conversion (those issue at a quarter of the FMA rate). Every step is an
+// explicit round-to-nearest operation, so no multiply-add is contracted.
+__device__ __forceinline__ void digits254(float t, uint32_t &a, uint32_t &b, uint32_t &c) {
+  const float M = 12582912.f;
+  const float ta = __fadd_rn(t, M), r1 = __fmul_rn(__fsub_rn(t, __fsub_rn(ta, M)), 254.f);
+  const float tb = __fadd_rn(r1, M), r2 = __fmul_rn(__fsub_rn(r1, __fsub_rn(tb, M)), 254.f);
+  const float tc = __fadd_rn(r2, M);
+  a = __float_as_uint(ta) & 255u;
+  b = __float_as_uint(tb) & 255u;
+  c = __float_as_uint(tc) & 255u;
+}
+
 // PRMT-based nibble/byte to float: 0x3F00_qq00_00 pattern gives 0.5 + q/256 for
 // q in [0, 255] placed in byte 2, i.e. an exact affine image of q. Summing
 // f*x and correcting with 0.5*sum(x) recovers sum(q*x) with fp32 rounding only.

@@ -626,7 +626,7 @@ static int enqueue_persist(wgd_ctx *ctx, int first, int start, int steps) {
   a.start = start;
   a.steps = steps;
   CK(cudaMemsetAsync(a.status, 0, 4 * sizeof(int), ctx->stream));
-  CK(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), ctx->stream));  // arrivals only; the generation word keeps counting
+  CK(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), ctx->stream));  // the arrival counter grows from 0 within a launch
   CK(launch_persist(a, ctx->sm_count, ctx->stream));
   CK(cudaMemcpyAsync(ctx->h_io + IO_STATUS, a.status, 4 * sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
   ctx->kernels = 1;
@@ -1472,7 +1472,7 @@ extern "C" int wgd_decode_sample(wgd_ctx *ctx, int32_t first, int start, int ste
   CK(cudaEventRecord(ctx->ev0, ctx->stream));
   for (int i = 0; i < steps; i++) {
     if (persist) {
-      CK(cudaMemsetAsync(pa.bar, 0, sizeof(unsigned), ctx->stream));  // arrivals only
+      CK(cudaMemsetAsync(pa.bar, 0, sizeof(unsigned), ctx->stream));  // arrival counter of this launch
       CK(launch_persist(pa, ctx->sm_count, ctx->stream));
       ctx->kernels = 1;
       if ((rc = enqueue_sample(ctx, ctx->d_step))) return rc;

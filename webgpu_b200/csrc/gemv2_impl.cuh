@@ -201,13 +201,11 @@ __device__ __forceinline__ void g2_digitise(const Gemv2Args &a, const G2Smem &S,
         uint32_t pk[3] = {0u, 0u, 0u};
 #pragma unroll
         for (int e = 0; e < 4; e++) {
-          const float t = xs[e] * sc;
-          const float fa = rintf(t), r1 = (t - fa) * 254.f;
-          const float fb = rintf(r1), r2 = (r1 - fb) * 254.f;
-          const float fc = rintf(r2);
-          pk[0] |= ((uint32_t)(int)fa & 255u) << (8 * e);
-          pk[1] |= ((uint32_t)(int)fb & 255u) << (8 * e);
-          pk[2] |= ((uint32_t)(int)fc & 255u) << (8 * e);
+          uint32_t da, db, dc;
+          digits254(xs[e] * sc, da, db, dc);
+          pk[0] |= da << (8 * e);
+          pk[1] |= db << (8 * e);
+          pk[2] |= dc << (8 * e);
         }
 #pragma unroll
         for (int dg = 0; dg < 3; dg++) {

@@ -128,6 +128,7 @@ struct PShared {
   float red[P_CWARPS];
   int dsum[P_CWARPS][48];  // digitiser scratch: one super-block's digit sums per warp
   float2 best[P_CWARPS + 1];
+  PPhase dsc[3];  // phase descriptors, a ring over the phase sequence: q, q + 1 (look-ahead), q + 2 (being copied)
   int flags[4];  // [0] stop (finished / winding down), [1] attention last-arriver, [2] token, [3] stop snapshot
 };
 // compute + epilogue warps / compute warps only
@@ -265,13 +266,11 @@ __device__ void p_digitise(const float *x, const float *nw, float eps, int cols,
       uint32_t pk[3] = {0u, 0u, 0u};
 #pragma unroll
       for (int e = 0; e < 4; e++) {
-        const float t = xs4[e] * sc;
-        const float fa = rintf(t), r1 = (t - fa) * 254.f;
-        const float fb = rintf(r1), r2 = (r1 - fb) * 254.f;
-        const float fc = rintf(r2);
-        pk[0] |= ((uint32_t)(int)fa & 255u) << (8 * e);
-        pk[1] |= ((uint32_t)(int)fb & 255u) << (8 * e);
-        pk[2] |= ((uint32_t)(int)fc & 255u) << (8 * e);
+        uint32_t da, db, dc;
+        digits254(xs4[e] * sc, da, db, dc);
+        pk[0] |= da << (8 * e);
+        pk[1] |= db << (8 * e);
+        pk[2] |= dc << (8 * e);
       }
 #pragma unroll
       for (int dg = 0; dg < 3; dg++) {
@@ -784,24 +783,20 @@ __device__ bool grid_sync(const PersistArgs &a, unsigned &gen, volatile int *sto
   }
 #endif
   if (threadIdx.x == 0 && !*stop) {
-    // the CTA's writes are ordered before thread 0's release by the barrier above
-    const unsigned g = gen;
-    unsigned prev;
-    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.bar) : "memory");
-    if (prev == gridDim.x - 1) {
-      asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(a.bar), "r"(0u) : "memory");
-      st_release(a.bar + 1, g + 1);
-    } else {
-      const uint64_t t0 = gtime();
-      for (unsigned it = 1; ld_acquire(a.bar + 1) == g; it++) {
-        if ((it & 63) == 0 && (*(volatile int *)a.status == 1 || gtime() - t0 > P_TIMEOUT_NS)) {
-          atomicCAS(a.status, 0, 1);
-          *stop = 1;
-          break;
-        }
+    // The CTA's writes are ordered before thread 0's release by the barrier above. The
+    // arrival counter only grows within a launch (zeroed before it): barrier number gen
+    // is complete when it reaches (gen + 1) * grid, which every CTA reads directly.
+    const unsigned target = (gen + 1u) * gridDim.x;
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
+    const uint64_t t0 = gtime();
+    for (unsigned it = 1; (int)(ld_acquire(a.bar) - target) < 0; it++) {
+      if ((it & 63) == 0 && (*(volatile int *)a.status == 1 || gtime() - t0 > P_TIMEOUT_NS)) {
+        atomicCAS(a.status, 0, 1);
+        *stop = 1;
+        break;
       }
     }
-    gen = g + 1;
+    gen++;
   }
 #ifdef WGD_PERSIST_TRACE
   if (threadIdx.x == 0 && tr_i >= 0 && tr_i < TR_BARS) g_bars[blockIdx.x][tr_i][1] = gtime();
@@ -887,6 +882,14 @@ __device__ void producer(const PersistArgs &a, const Ring &R, volatile int *stop
   }
 }
 
+// One warp copies a phase descriptor from the plan in global memory into shared memory.
+__device__ __forceinline__ void p_copy_phase(PPhase *dst, const PPhase *src, int lane) {
+  static_assert(sizeof(PPhase) % 4 == 0, "descriptor copied in words");
+  const uint32_t *s = reinterpret_cast<const uint32_t *>(src);
+  uint32_t *d = reinterpret_cast<uint32_t *>(dst);
+  for (int i = lane; i < (int)(sizeof(PPhase) / 4); i += 32) d[i] = __ldg(s + i);
+}
+
 __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   Ring R;
@@ -922,9 +925,13 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
   // ---------------- compute warps (0..7) and the epilogue warp (8)
   const bool comp = warp < P_CWARPS, epi = warp == P_EWARP;
   const int grid = gridDim.x, c = blockIdx.x;
-  unsigned gen = 0;
-  if (tid == 0) gen = ld_acquire(a.bar + 1);
+  unsigned gen = 0;  // grid barriers passed in this launch (thread 0)
   unsigned g = 0;  // ring stage counter, in step with the producer
+  // the first two phase descriptors; later ones are copied one phase ahead of use
+  if (epi) {
+    p_copy_phase(&sh.dsc[0], a.phases, lane);
+    p_copy_phase(&sh.dsc[1], a.phases + (a.nphases > 1 ? 1 : 0), lane);
+  }
   int token = a.dev_first ? __ldcg(a.dev_first) : a.first;
   const int start = a.dev_start ? __ldcg(a.dev_start) : a.start;
   bool att_staged = false;  // attention stage 0 was filled during the previous phase
@@ -939,7 +946,9 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
     if (!grid_sync(a, gen, stop)) break;
     bool alive = true;
     for (int p = 0; p < a.nphases && alive; p++) {
-      const PPhase &ph = a.phases[p];
+      const int q = step * a.nphases + p;  // position in the phase sequence of the launch
+      const PPhase &ph = sh.dsc[q % 3];
+      if (epi) p_copy_phase(&sh.dsc[(q + 2) % 3], a.phases + (p + 2) % a.nphases, lane);
       if (tid == 0) P_TRACE(step, p, 0);
       if (ph.kind == PH_ATTN) {
         const PAttn &A = ph.a;
@@ -963,8 +972,8 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
       if (comp) {
         // when attention follows, warps 0..3 start copying this CTA's first K/V tile now
         // (rows of earlier positions only) into attention stage 0, above the digit records
-        if (p + 1 < a.nphases && a.phases[p + 1].kind == PH_ATTN && warp < 4) {
-          const PAttn &A = a.phases[p + 1].a;
+        if (p + 1 < a.nphases && sh.dsc[(q + 1) % 3].kind == PH_ATTN && warp < 4) {
+          const PAttn &A = sh.dsc[(q + 1) % 3].a;
           if (px_bytes(pg.cols) <= (size_t)attn_stage_floats(A.hd) * 4) {
             int chunk, nsp;
             attn_split(A, pos, a.nsp_max, chunk, nsp);

@@ -66,7 +66,7 @@ struct PersistArgs {
   float *att_part;      // [kv_heads][nsp_max][group][hd + 4]
   unsigned *att_ctr;    // [kv_heads] (zero, left zero)
   float2 *cand;         // [grid] (best logit, index bits) of each CTA
-  unsigned *bar;        // grid barrier: [0] arrivals (zero at launch), [1] generation
+  unsigned *bar;        // grid barrier: [0] arrivals, zero at launch and growing by grid per barrier
   int *status;          // [0] 0 ok, 1 wait limit hit, 2 non-finite logits, 3 cancelled; [1] steps done
   int nstage, xs_bytes, nsp_max;
   int l2_ahead;  // ring stages requested into L2 ahead of the shared-memory copies (0: none)
