@@ -257,7 +257,9 @@ __device__ void p_digitise(const float *x, const float *nw, float eps, int cols,
     for (int p = 0; p < 2; p++)
       amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i][p].x), fabsf(v[i][p].y)), fmaxf(fabsf(v[i][p].z), fabsf(v[i][p].w))));
     amax = warp_max(amax);
-    const float sc = amax > 0.f ? 127.f / amax : 0.f;
+    // digit scale: the fast reciprocal is within 2 ulp of 127 / amax, which only moves the
+    // digits by that much relative to the exact scale sxs they are multiplied back with
+    const float sc = amax > 0.f ? __fdividef(127.f, amax) : 0.f;
     if (lane == 0) X.sxs[sb] = amax > 0.f ? amax / 127.f : 0.f;
 #pragma unroll
     for (int p = 0; p < 2; p++) {
@@ -544,6 +546,12 @@ __device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, in
   if (!staged) p_attn_stage(A, pos, kh, p1, p0, sm, 0, tid);
   if (ntiles > 1) p_attn_stage(A, pos, kh, p1, p0 + 32, sm, 1, tid);
   const int hq = G + (owns_new ? 1 : 0);
+  // this lane's RoPE (cos, sin) pairs, requested together with q/k/v (the same for every head)
+  const int half = A.rot / 2;
+  const float2 *tb = A.table + (int64_t)pos * half;
+  float2 cs[4];
+#pragma unroll
+  for (int k = 0; k < 4; k++) cs[k] = lane + 32 * k < half ? __ldg(tb + lane + 32 * k) : make_float2(1.f, 0.f);
   for (int i = tid; i < hq * hd; i += 128) {
     const int g = i / hd, d = i - g * hd;
     const float *src = g < G ? A.qkv + (int64_t)(kh * G + g) * hd : A.qkv + (int64_t)(A.heads + kh) * hd;
@@ -563,14 +571,14 @@ __device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, in
       for (int d = lane; d < hd; d += 32) hv[d] = hv[d] * inv * nw[d];
       __syncwarp();
     }
-    const int half = A.rot / 2;
-    const float2 *tb = A.table + (int64_t)pos * half;
-    for (int i = lane; i < half; i += 32) {
-      const float2 cs = __ldg(tb + i);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int i = lane + 32 * k;
+      if (i >= half) break;
       const int ia = A.mode == 0 ? i : 2 * i, ib = A.mode == 0 ? i + half : 2 * i + 1;
       const float l = hv[ia], r = hv[ib];
-      hv[ia] = l * cs.x - r * cs.y;
-      hv[ib] = l * cs.y + r * cs.x;
+      hv[ia] = l * cs[k].x - r * cs[k].y;
+      hv[ib] = l * cs[k].y + r * cs[k].x;
     }
     __syncwarp();
   }
@@ -701,12 +709,18 @@ __device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, in
     for (int i = 0; i < 2; i++) {
       const int d4 = lane + 32 * i;
       float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-      for (int j = 0; j < nsp; j++) {
-        const float w = __shfl_sync(0xffffffffu, j < 32 ? wa : wb, j & 31);
-        if (d4 < hd4) {
-          const float4 pv = __ldcg(reinterpret_cast<const float4 *>(ph + j * sstride) + d4);
-          num = make_float4(fmaf(w, pv.x, num.x), fmaf(w, pv.y, num.y), fmaf(w, pv.z, num.z), fmaf(w, pv.w, num.w));
+      // the split partials in batches of 8 independent loads (one L2 round trip per batch)
+      for (int j0 = 0; j0 < nsp; j0 += 8) {
+        float4 pv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+          pv[u] = j0 + u < nsp && d4 < hd4 ? __ldcg(reinterpret_cast<const float4 *>(ph + (j0 + u) * sstride) + d4)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          const int j = j0 + u;  // splits past nsp have weight 0 and a zero partial
+          const float w = __shfl_sync(0xffffffffu, j < 32 ? wa : wb, j & 31);
+          num = make_float4(fmaf(w, pv[u].x, num.x), fmaf(w, pv[u].y, num.y), fmaf(w, pv[u].z, num.z), fmaf(w, pv[u].w, num.w));
         }
       }
       if (d4 < hd4) reinterpret_cast<float4 *>(out_base + g * hd)[d4] = make_float4(num.x / den, num.y / den, num.z / den, num.w / den);
