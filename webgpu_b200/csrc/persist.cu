@@ -80,9 +80,6 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release(unsigned *p, unsigned v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 __device__ __forceinline__ void cp_async16(void *smem, const void *g) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(su32(smem)), "l"(g) : "memory");
 }
@@ -507,18 +504,21 @@ __device__ __forceinline__ float *attn_stage(float *sm, int hd, int st) { return
 // Issue the cp.async copies of K/V rows [tile, min(tile + 32, p1)) of kv head kh into stage st
 // (the row of the position being decoded comes from shared memory instead) and commit them.
 __device__ void p_attn_stage(const PAttn &A, int pos, int kh, int p1, int tile, float *sm, int st, int tid) {
-  const int hd = A.hd, hd4 = hd >> 2, RS = hd + 4, end = pos + 1;
+  const int hd = A.hd, RS = hd + 4, end = pos + 1;
   const bool owns_new = p1 == end;
   const float *kb = A.k + (int64_t)kh * A.capacity * hd, *vb = A.v + (int64_t)kh * A.capacity * hd;
-  const int cnt = min(32, p1 - tile), total = cnt * hd4;
+  const int cnt = min(32, p1 - tile);
   float *ks = attn_stage(sm, hd, st), *vs = ks + 32 * RS;
-  for (int i = tid; i < total; i += 128) {
-    const int r = i / hd4, c = (i - r * hd4) * 4;
+  // a warp per key row (the ring slot computed once per row), lanes over its 16-byte pieces
+  const int w = tid >> 5, lane = tid & 31;
+  for (int r = w; r < cnt; r += 4) {
     const int p = tile + r;
     if (owns_new && p == end - 1) continue;
     const int64_t row = (int64_t)(p % A.capacity) * hd;
-    cp_async16(ks + r * RS + c, kb + row + c);
-    cp_async16(vs + r * RS + c, vb + row + c);
+    for (int c = 4 * lane; c < hd; c += 128) {
+      cp_async16(ks + r * RS + c, kb + row + c);
+      cp_async16(vs + r * RS + c, vb + row + c);
+    }
   }
   cp_commit();
 }
@@ -698,6 +698,7 @@ __device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, in
   const int64_t sstride = (int64_t)G * PR;
   for (int g = warp; g < G; g += 4) {
     const float *ph = pb + g * PR;
+    // the first batch of partial vectors goes out with the (m, l) loads: one round trip for both
     const float ma = lane < nsp ? __ldcg(ph + lane * sstride + hd) : -FLT_MAX;
     const float mb = lane + 32 < nsp ? __ldcg(ph + (lane + 32) * sstride + hd) : -FLT_MAX;
     const float M = warp_max(fmaxf(ma, mb));
@@ -715,7 +716,7 @@ __device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, in
 #pragma unroll
         for (int u = 0; u < 8; u++)
           pv[u] = j0 + u < nsp && d4 < hd4 ? __ldcg(reinterpret_cast<const float4 *>(ph + (j0 + u) * sstride) + d4)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int u = 0; u < 8; u++) {
           const int j = j0 + u;  // splits past nsp have weight 0 and a zero partial
