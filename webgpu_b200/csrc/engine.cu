@@ -497,6 +497,7 @@ static int build_persist_plan(wgd_ctx *ctx) {
   if (c.family == 1) return no("the gemma block (post-norms) uses the per-kernel path");
   const int G = ctx->kv_l ? ctx->heads_l / ctx->kv_l : 0;
   if (hd % 4 || hd > 256 || G < 1 || G > 8) return no("attention shape outside the persistent kernel");
+  // at least 8 super-blocks per row: the kernel's epilogue warp folds at most two tile ends per ring stage
   auto tiled_ok = [](const DevLinear &L) { return L.tiled && L.cols % 256 == 0 && L.cols / 256 >= 8; };
   if (!tiled_ok(ctx->lm)) return no("the LM head is not in the tiled layout");
   int max_cols = H;

@@ -1068,18 +1068,24 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
             for (int j = 0; j < P_STAGE_UNITS; j++) v[j] = (j < n && lane < 16) ? sh.res[rs][j][lane] : 0.f;
             __syncwarp();
             if (lane == 0) mbar_arrive(R.resfree + rs);  // results copied out
+            // the stage's results in k-block order; a tile ends where the running k-block count
+            // reaches nkb. With n <= 16 results and nkb >= 8 (inputs >= 2048 wide) a stage holds at
+            // most two tile ends, so the sums run branch-free and the epilogue is emitted after
+            // the loop (the same additions in the same order as one epilogue per result)
+            const int e1 = nkb - 1 - kbe, e2 = e1 + nkb;
+            float o1 = 0.f, o2 = 0.f;
 #pragma unroll
             for (int j = 0; j < P_STAGE_UNITS; j++) {
               if (j < n) {
                 run += v[j];
-                if (++kbe == nkb) {
-                  p_epilogue(C, t, run, lane);
-                  run = 0.f;
-                  kbe = 0;
-                  t++;
-                }
+                if (j == e1) { o1 = run; run = 0.f; }
+                if (j == e2) { o2 = run; run = 0.f; }
               }
             }
+            if (e1 < n) p_epilogue(C, t++, o1, lane);
+            if (e2 < n) p_epilogue(C, t++, o2, lane);
+            kbe += n;
+            while (kbe >= nkb) kbe -= nkb;
           } else {
             __syncwarp();
             if (lane == 0) mbar_arrive(R.resfree + rs);
