@@ -6,6 +6,7 @@
     python -m webgpu_b200.probe decode LAYERS STEPS [PERSISTENT]  # Llama-3-8B-width model, wgd_decode
     python -m webgpu_b200.probe gemm ROWS COLS BATCH [LAUNCHES] [TYPE]  # wgd_op_gemm_tiled vs the GEMV (TYPE 12 Q4_K, 14 Q6_K)
     python -m webgpu_b200.probe prefill LAYERS BATCH [MIN_BATCH]  # Llama-3-8B-width prompt batches
+    python -m webgpu_b200.probe qwen STEPS [REPEATS]              # Qwen2.5-0.5B architecture, wgd_decode
 
 `gemv` repacks random GGUF blocks of TYPE (12 = Q4_K, 14 = Q6_K) into the tile layout once and calls the
 tiled GEMV LAUNCHES times (default 5). `attention` keeps 24 K/V caches of [8][4096][128] fp32 (more than
@@ -150,6 +151,30 @@ def prefill(layers: int, batch: int, min_batch: int = 16) -> None:
     e.dispose()
 
 
+def qwen(steps: int, repeats: int = 3) -> None:
+    """The Qwen2.5-0.5B benchmark configuration: 23-token prompt in one batch, then `wgd_decode` of
+    STEPS tokens REPEATS times (the first call also captures the per-kernel step graph)."""
+    from .engine import PagedEngine
+    from .source import MemorySource
+    spec = synth.baseline_spec(2)
+    img = synth.build_gguf(spec)
+    e = PagedEngine()
+    e.load(MemorySource(img), {"contextLength": 512, "batchSize": 32, "performance": "fast"})
+    L = _native.lib()
+    prompt = list(spec.prompt)
+    tok = e.forward(prompt, 0, True)
+    buf = (ctypes.c_int32 * steps)()
+    st = _native.StatsC()
+    per = ctypes.c_int(0)
+    for _ in range(repeats):
+        _native.check(L.wgd_decode(e.ctx, tok, len(prompt), steps, buf))
+        _native.check(L.wgd_stats_get(e.ctx, ctypes.byref(st)))
+        _native.check(L.wgd_kernels_per_token(e.ctx, ctypes.byref(per)))
+        print(f"qwen2.5-0.5b: {st.last_forward_ms / steps * 1000:.1f} us/token ({steps} steps); {per.value} kernels per token",
+              flush=True)
+    e.dispose()
+
+
 def main(argv):
     if not argv:
         print(__doc__)
@@ -165,6 +190,8 @@ def main(argv):
         gemm(*args)
     elif cmd == "prefill":
         prefill(*args)
+    elif cmd == "qwen":
+        qwen(*args)
     else:
         print(__doc__)
         return 2
