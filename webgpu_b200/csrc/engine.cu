@@ -129,8 +129,8 @@ struct wgd_ctx {
   float *hidden = nullptr, *qkv = nullptr, *qrot = nullptr, *att = nullptr, *proj = nullptr, *act = nullptr, *logits = nullptr;
   int *d_ids = nullptr, *d_start = nullptr, *d_argmax = nullptr, *d_err = nullptr;
   float *d_maxval = nullptr, *att_part = nullptr, *am_part = nullptr;
-  unsigned *att_ctr = nullptr, *gemv_ctr = nullptr, *am_ctr = nullptr;
-  int att_splits = 1, gemv_slot = 0;
+  unsigned *att_ctr = nullptr, *am_ctr = nullptr;
+  int att_splits = 1;
   uint8_t *staging = nullptr;
   size_t staging_bytes = 0;
   std::vector<std::pair<std::pair<double, double>, float2 *>> rope_tables;  // (theta, scale) -> table
@@ -805,7 +805,6 @@ extern "C" int wgd_model_end(wgd_ctx *ctx) {
   if ((rc = ctx_alloc_t(ctx, &ctx->att_part, attention_part_floats(B, c.heads / tp, ctx->kv_l, hd, ctx->att_splits), "attention partials")))
     return rc;
   if ((rc = ctx_alloc_t(ctx, &ctx->att_ctr, (size_t)B * ctx->kv_l, "attention counters"))) return rc;
-  if ((rc = ctx_alloc_t(ctx, &ctx->gemv_ctr, 2 * 1024, "gemv counters"))) return rc;
   if ((rc = ctx_alloc_t(ctx, &ctx->am_part, 2 * 256, "argmax partials")) || (rc = ctx_alloc_t(ctx, &ctx->am_ctr, 4, "argmax counter")))
     return rc;
   if ((rc = ctx_alloc_t(ctx, &ctx->d_sparams, 1, "sampling settings")) ||
@@ -1097,7 +1096,6 @@ static int gemv(wgd_ctx *ctx, const DevLinear &L, const float *x, int ldx, const
   a.bias = bias;
   a.epi = epi;
   a.batch = batch;
-  a.ctr = ctx->gemv_ctr + 2 * (ctx->gemv_slot++ % 1024);
   CK(launch_gemv(L.type, a, ctx->stream, true, ctx->sm_count));
   return WGD_OK;
 }
@@ -1115,7 +1113,6 @@ static int enqueue_forward(wgd_ctx *ctx, int n, bool want_logits_rows, bool io =
   const int H = c.hidden, hd = c.head_dim;
   const bool gemma = c.family == 1, tp1 = ctx->tp_size == 1;
   int rc;
-  ctx->gemv_slot = 0;
   ctx->kernels = 0;
   if (io) {
     CK(cudaMemcpyAsync(ctx->d_start, ctx->h_io, sizeof(int32_t), cudaMemcpyHostToDevice, ctx->stream));
@@ -1645,9 +1642,9 @@ extern "C" int wgd_op_gemv(int type, int64_t rows, int64_t cols, const void *pac
   if (!type_supported(type) || cols % block_elems(type) || cols % 32 || rows < 1 || batch < 1)
     return fail(WGD_EINVAL, "bad type, shape or batch");
   if (gemv_max_batch((int)cols) == 0) return fail(WGD_EINVAL, "matrix too wide for the GEMV kernel");
-  unsigned *ctr;
+  unsigned *unused;
   int sm, rc;
-  if ((rc = op_scratch(&ctr, &sm))) return rc;
+  if ((rc = op_scratch(&unused, &sm))) return rc;  // caches the SM count of this device
   GemvArgs a{};
   a.w = (const uint8_t *)packed;
   a.drow = dev_row_bytes(type, cols);
@@ -1660,7 +1657,6 @@ extern "C" int wgd_op_gemv(int type, int64_t rows, int64_t cols, const void *pac
   a.ldy = (int)rows;
   a.epi = EPI_STORE;
   a.batch = batch;
-  a.ctr = ctr;
   CK(launch_gemv(type, a, (cudaStream_t)stream, false, sm));
   return WGD_OK;
 }

@@ -9,8 +9,10 @@
 //     instruction reads a contiguous span of quant bytes with 16-byte loads).
 //   * Each lane keeps the activations of its units in registers for the whole
 //     kernel (loaded once per CTA, optionally RMS-normalised on the way in).
-//   * CTAs are persistent and pull 4-row work items from a ticket counter, so
-//     the tail is balanced at 4-row granularity whatever the matrix shape.
+//   * CTAs are persistent and take 4-row work items round-robin (the grid is
+//     at most the resident capacity and the item count), so the tail is balanced
+//     at 4-row granularity whatever the matrix shape; the first item's weight
+//     rows are prefetched into L2 before the wait on the previous kernel.
 //   * Per item, each warp reduces its 4*NB partial sums with a transposed
 //     butterfly, the CTA combines warps in shared memory, and the epilogue
 //     (store / residual add / SiLU / gated SiLU or GELU) writes the outputs.
@@ -55,40 +57,33 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvArgs a) {
   __shared__ float red[2][8][V];
   __shared__ float s_norm[8][NB];
   __shared__ float s_inv[NB];
-  __shared__ int s_item[2];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
 
+  // Work items of 4 rows, round-robin over the CTAs (all resident; the grid never exceeds the
+  // item count). The weights do not depend on earlier kernels: this CTA's first item goes to
+  // L2 while the previous kernel finishes, and each later item while the one before it runs.
+  const int items = (a.rows + RB - 1) / RB;
+  auto prefetch_item = [&](int item) {
+    for (int r = 0; r < RB; r++) {
+      const int row = item * RB + r;
+      if (row < a.rows)
+        for (int off = tid * 16; off < a.drow; off += (int)blockDim.x * 16)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(a.w + (int64_t)row * a.drow + off));
+    }
+  };
+  prefetch_item((int)blockIdx.x);
   pdl_wait();
-  if (tid == 0) s_item[0] = (int)atomicAdd(a.ctr, 1u);
 
-  // Fused RMSNorm of the activation rows (normShader semantics: x * rsqrt(mean(x^2)+eps) * w).
-  if (a.norm_w) {
-#pragma unroll
-    for (int b = 0; b < NB; b++) {
-      float s = 0.f;
-      if (b < a.batch) {
-        const float4 *xr = reinterpret_cast<const float4 *>(a.x + (int64_t)b * a.ldx);
-        for (int c = tid; c < (a.cols >> 2); c += blockDim.x) {
-          float4 v = __ldg(xr + c);
-          s = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, s))));
-        }
-      }
-      s = warp_sum(s);
-      if (lane == 0) s_norm[warp][b] = s;
-    }
-    __syncthreads();
-    if (tid < NB) {
-      float t = 0.f;
-      for (int w = 0; w < nwarp; w++) t += s_norm[w][tid];
-      s_inv[tid] = rsqrtf(t / (float)a.cols + a.eps);
-    }
-  }
-  __syncthreads();
-
-  // Activations of this lane's units, in registers for the whole kernel.
+  // Activations of this lane's units, in registers for the whole kernel (the CTA's units cover
+  // the whole row). One round of loads: x and, for the fused RMSNorm (normShader semantics:
+  // x * rsqrt(mean(x^2)+eps) * w), its weight; the norm's sum of squares comes from the same
+  // registers, and the 1/rms factor scales x*w once the CTA has the sum.
   XUnit xu[UPL][NB];
   int uidx[UPL];
   bool uval[UPL];
+  float ss[NB];
+#pragma unroll
+  for (int b = 0; b < NB; b++) ss[b] = 0.f;
 #pragma unroll
   for (int k = 0; k < UPL; k++) {
     const int u = (warp * UPL + k) * 32 + lane;
@@ -99,35 +94,65 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvArgs a) {
 #pragma unroll
     for (int b = 0; b < NB; b++) {
       XUnit &X = xu[k][b];
-      float sa = 0.f, sb = 0.f;
       const bool live = uval[k] && b < a.batch;
       const float *xr = a.x + (int64_t)b * a.ldx;
-      const float inv = a.norm_w ? s_inv[b] : 1.f;
 #pragma unroll
       for (int i = 0; i < 16; i += 4) {
         float4 va = live ? __ldg(reinterpret_cast<const float4 *>(xr + ca + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
         float4 vb = live ? __ldg(reinterpret_cast<const float4 *>(xr + cb + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        if (a.norm_w && live) {
-          float4 wa = __ldg(reinterpret_cast<const float4 *>(a.norm_w + ca + i));
-          float4 wb = __ldg(reinterpret_cast<const float4 *>(a.norm_w + cb + i));
-          va = make_float4(va.x * inv * wa.x, va.y * inv * wa.y, va.z * inv * wa.z, va.w * inv * wa.w);
-          vb = make_float4(vb.x * inv * wb.x, vb.y * inv * wb.y, vb.z * inv * wb.z, vb.w * inv * wb.w);
+        if (a.norm_w) {
+          ss[b] = fmaf(va.x, va.x, fmaf(va.y, va.y, fmaf(va.z, va.z, fmaf(va.w, va.w, ss[b]))));
+          ss[b] = fmaf(vb.x, vb.x, fmaf(vb.y, vb.y, fmaf(vb.z, vb.z, fmaf(vb.w, vb.w, ss[b]))));
+          if (live) {
+            const float4 wa = __ldg(reinterpret_cast<const float4 *>(a.norm_w + ca + i));
+            const float4 wb = __ldg(reinterpret_cast<const float4 *>(a.norm_w + cb + i));
+            va = make_float4(va.x * wa.x, va.y * wa.y, va.z * wa.z, va.w * wa.w);
+            vb = make_float4(vb.x * wb.x, vb.y * wb.y, vb.z * wb.z, vb.w * wb.w);
+          }
         }
         X.a[i] = va.x; X.a[i + 1] = va.y; X.a[i + 2] = va.z; X.a[i + 3] = va.w;
         X.b[i] = vb.x; X.b[i + 1] = vb.y; X.b[i + 2] = vb.z; X.b[i + 3] = vb.w;
-        sa += (va.x + va.y) + (va.z + va.w);
-        sb += (vb.x + vb.y) + (vb.z + vb.w);
+      }
+    }
+  }
+  if (a.norm_w) {
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+      const float t = warp_sum(ss[b]);
+      if (lane == 0) s_norm[warp][b] = t;
+    }
+    __syncthreads();
+    if (tid < NB) {
+      float t = 0.f;
+      for (int w = 0; w < nwarp; w++) t += s_norm[w][tid];
+      s_inv[tid] = rsqrtf(t / (float)a.cols + a.eps);
+    }
+  }
+  __syncthreads();  // s_inv
+#pragma unroll
+  for (int k = 0; k < UPL; k++) {
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+      XUnit &X = xu[k][b];
+      const float inv = a.norm_w ? s_inv[b] : 1.f;
+      float sa = 0.f, sb = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        if (a.norm_w) {
+#pragma unroll
+          for (int e = 0; e < 4; e++) { X.a[i + e] *= inv; X.b[i + e] *= inv; }
+        }
+        sa += (X.a[i] + X.a[i + 1]) + (X.a[i + 2] + X.a[i + 3]);
+        sb += (X.b[i] + X.b[i + 1]) + (X.b[i + 2] + X.b[i + 3]);
       }
       X.sa = sa; X.sb = sb;
     }
   }
   pdl_launch_dependents();
 
-  const int items = (a.rows + RB - 1) / RB;
   int buf = 0;
-  int item = s_item[0];
-  while (item < items) {
-    if (tid == 0) s_item[buf ^ 1] = (int)atomicAdd(a.ctr, 1u);
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    if (item + (int)gridDim.x < items) prefetch_item(item + (int)gridDim.x);
     const int row0 = item * RB;
     float acc[V];
 #pragma unroll
@@ -174,17 +199,12 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvArgs a) {
         }
       }
     }
-    item = s_item[buf ^ 1];
     buf ^= 1;
   }
+  // every epilogue store of the CTA performed at device scope before it exits (without this
+  // the kernel that follows under programmatic dependent launch read stale outputs)
   __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    if (atomicAdd(a.ctr + 1, 1u) == gridDim.x - 1) {
-      a.ctr[0] = 0u;
-      a.ctr[1] = 0u;
-    }
-  }
+  if (tid == 0) __threadfence();
 }
 
 template <int T, int NB, int UPL>

@@ -33,7 +33,6 @@ struct GemvArgs {
   const float *bias;  // [rows] in device row order, or null
   int epi;
   int batch;          // number of activation rows
-  unsigned *ctr;      // 2 x uint32, zero on entry and on exit
 };
 cudaError_t launch_gemv(int type, const GemvArgs &a, cudaStream_t s, bool pdl, int sm_count);
 // Largest batch chunk the register-resident GEMV handles for this width in one pass.
