@@ -430,7 +430,7 @@ __device__ __forceinline__ void emit(const TcArgs &a, int row, int b, float v, f
   } else {
     if (row >= a.rows) return;
     float *dst = a.y + (int64_t)b * a.ldy + row;
-    if constexpr (EPI == EPI_ADD) *dst += v + brow;
+    if constexpr (EPI == EPI_ADD) *dst = __ldcg(dst) + (v + brow);  // residual read through L2
     else if constexpr (EPI == EPI_SILU) *dst = tc_silu(v + brow);
     else *dst = v + brow;
   }
@@ -553,7 +553,7 @@ __device__ void emit16(const TcArgs &a, int row0, int b, const float (&v)[16]) {
       float x = v[j];
       if (a.bias) x += __ldg(a.bias + row);
       float *dst = a.y + (int64_t)b * a.ldy + row;
-      if constexpr (EPI == EPI_ADD) *dst += x;
+      if constexpr (EPI == EPI_ADD) *dst = __ldcg(dst) + x;
       else if constexpr (EPI == EPI_SILU) *dst = tc_silu(x);
       else *dst = x;
     }

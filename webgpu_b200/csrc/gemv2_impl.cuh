@@ -456,7 +456,7 @@ __device__ __forceinline__ void g2_store(const Gemv2Args &a, int t, int grp, con
       float val = v[b][i];
       if (a.bias) val += __ldg(a.bias + row);
       float *dst = a.y + (int64_t)b * a.ldy + row;
-      if (a.epi == EPI_ADD) *dst += val;
+      if (a.epi == EPI_ADD) *dst = __ldcg(dst) + val;  // through L2, so that no stale line stays in L1
       else if (a.epi == EPI_SILU) *dst = g2_silu(val);
       else *dst = val;
     }

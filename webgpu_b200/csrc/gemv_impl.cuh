@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvArgs a) {
         } else if (row < a.rows) {
           if (a.bias) val += __ldg(a.bias + row);
           float *dst = a.y + (int64_t)b * a.ldy + row;
-          if (a.epi == EPI_ADD) *dst += val;
+          if (a.epi == EPI_ADD) *dst = __ldcg(dst) + val;  // through L2: see the end of the kernel
           else if (a.epi == EPI_SILU) *dst = silu_f(val);
           else *dst = val;
         }
@@ -201,8 +201,11 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvArgs a) {
     }
     buf ^= 1;
   }
-  // every epilogue store of the CTA performed at device scope before it exits (without this
-  // the kernel that follows under programmatic dependent launch read stale outputs)
+  // Under programmatic dependent launch the next kernel's CTAs may already be resident on this
+  // SM, past the point where a kernel boundary would have invalidated its L1, so no line of an
+  // output that other SMs update may stay in this SM's L1: residual reads go through L2 (above),
+  // and the device-scope fence at the end also invalidates the L1 (without it a Q8_0 model's
+  // logits came out 12-25 % off).
   __syncthreads();
   if (tid == 0) __threadfence();
 }

@@ -191,7 +191,7 @@ __global__ void rmsnorm_kernel(const float *x, int ldx, const float *w, float ep
   const float inv = rsqrtf(block_sum(s, sh) / (float)cols + eps);
   for (int c = threadIdx.x; c < cols; c += blockDim.x) {
     const float v = xr[c] * inv * w[c];
-    if (add) yr[c] += v; else yr[c] = v;
+    if (add) yr[c] = __ldcg(yr + c) + v; else yr[c] = v;  // residual read through L2
   }
   pdl_launch_dependents();
 }
@@ -882,7 +882,7 @@ cudaError_t launch_advance(int *ids, int *start, const int *argmax, int *tokens,
 
 __global__ void add_kernel(const float *x, float *y, int64_t n) {
   pdl_wait();
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) y[i] += x[i];
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) y[i] = __ldcg(y + i) + x[i];
   pdl_launch_dependents();
 }
 cudaError_t launch_add(const float *x, float *y, int64_t n, cudaStream_t s, bool pdl) {

@@ -193,7 +193,7 @@ __global__ void allreduce_kernel(const TpDev d, const float *partial, float *out
   for (size_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
     float s = 0.f;
     for (int j = 0; j < d.size; j++) s += __ldcg(slots + (size_t)j * d.cap + i);
-    out[i] = add ? out[i] + s : s;
+    out[i] = add ? __ldcg(out + i) + s : s;  // residual read through L2
   }
   finish(d, e);
   pdl_launch_dependents();

@@ -7,6 +7,7 @@
     python -m webgpu_b200.probe gemm ROWS COLS BATCH [LAUNCHES] [TYPE]  # wgd_op_gemm_tiled vs the GEMV (TYPE 12 Q4_K, 14 Q6_K)
     python -m webgpu_b200.probe prefill LAYERS BATCH [MIN_BATCH]  # Llama-3-8B-width prompt batches
     python -m webgpu_b200.probe qwen STEPS [REPEATS]              # Qwen2.5-0.5B architecture, wgd_decode
+    python -m webgpu_b200.probe gemma_paged LAYERS STEPS          # Gemma-3-27B widths, 2 GiB budget, paged
 
 `gemv` repacks random GGUF blocks of TYPE (12 = Q4_K, 14 = Q6_K) into the tile layout once and calls the
 tiled GEMV LAUNCHES times (default 5). `attention` keeps 24 K/V caches of [8][4096][128] fp32 (more than
@@ -175,6 +176,57 @@ def qwen(steps: int, repeats: int = 3) -> None:
     e.dispose()
 
 
+def gemma_paged(layers: int, steps: int) -> None:
+    """Gemma-3-27B widths (seed 3) with LAYERS layers under a 2 GiB engine budget and 16 MiB pages
+    (`low-memory`): the matrices that do not fit stream from pinned host memory through the two
+    device page slots every forward. Prefills a 1024-token prompt in batches of 128, then times
+    `wgd_decode` of STEPS tokens; reports the bytes streamed per token against a pinned
+    host-to-device copy measured in the same process."""
+    import time
+
+    import torch
+
+    from .engine import PagedEngine
+    from .source import MemorySource
+    t0 = time.time()
+    spec = synth.baseline_spec(4, layers=layers)
+    img = synth.build_gguf(spec)
+    print(f"gemma-3-27b widths, {layers} layers: {img.nbytes / 1e9:.2f} GB GGUF built in {time.time() - t0:.1f}s", flush=True)
+    e = PagedEngine()
+    t0 = time.time()
+    e.load(MemorySource(img), {"contextLength": 2048, "batchSize": 128, "performance": "low-memory", "gpuBudgetMiB": 2048})
+    st = _native.StatsC()
+    L = _native.lib()
+    _native.check(L.wgd_stats_get(e.ctx, ctypes.byref(st)))
+    print(f"loaded in {time.time() - t0:.1f}s; device bytes {st.gpu_bytes / 1e9:.2f} GB", flush=True)
+    prompt = list(synth.uniform_ids(1024, 262144, seed=3))
+    tok, pf = None, 0.0
+    for i in range(0, 1024, 128):
+        tok = e.forward(prompt[i:i + 128], i, i + 128 == 1024)
+        _native.check(L.wgd_stats_get(e.ctx, ctypes.byref(st)))
+        pf += st.last_forward_ms
+    print(f"prefill 1024 tokens in batches of 128: {pf:.0f} ms", flush=True)
+    buf = (ctypes.c_int32 * steps)()
+    _native.check(L.wgd_decode(e.ctx, tok, 1024, steps, buf))
+    _native.check(L.wgd_stats_get(e.ctx, ctypes.byref(st)))
+    per = st.last_forward_ms / steps
+    streamed = st.streamed_bytes / steps
+    print(f"decode: {per:.1f} ms/token ({1000 / per:.2f} tok/s); {streamed / 1e9:.2f} GB streamed per token = "
+          f"{streamed / per / 1e6:.1f} GB/s", flush=True)
+    e.dispose()
+    h = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    d = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+    for _ in range(2):
+        d.copy_(h, non_blocking=True)
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(4):
+        d.copy_(h, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    print(f"pinned host-to-device copy: {4 * (1 << 30) / (e0.elapsed_time(e1) / 1000) / 1e9:.1f} GB/s", flush=True)
+
+
 def main(argv):
     if not argv:
         print(__doc__)
@@ -192,6 +244,8 @@ def main(argv):
         prefill(*args)
     elif cmd == "qwen":
         qwen(*args)
+    elif cmd == "gemma_paged":
+        gemma_paged(*args)
     else:
         print(__doc__)
         return 2
