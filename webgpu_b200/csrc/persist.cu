@@ -9,14 +9,14 @@
 //
 // Synchronisation:
 //  * between phases, a grid barrier (all CTAs are co-resident: cooperative
-//    launch, one CTA per SM) with an arrival counter and a generation word;
+//    launch, one CTA per SM) with one arrival counter that only grows;
 //  * inside a CTA, the producer warp and the consumer warps share a ring of
 //    shared-memory slots guarded by mbarriers ("full": transaction bytes of the
 //    bulk copy; "empty": one arrival per consumer warp);
-//  * a 16-row output tile whose units are spread over the CTA's warps is
-//    summed in warp order by the warp that publishes last; a tile cut between
-//    CTAs is finished by the CTA that arrives last, summing in CTA order, so
-//    every sum has a fixed order.
+//  * each CTA owns whole 16-row output tiles; the compute warps hand each
+//    chunk's 16 row sums to the epilogue warp through a ring of result stages
+//    (mbarriers "done" / "resfree"), and the epilogue warp adds a tile's chunks
+//    in k-block order, so every sum has a fixed order.
 // Every wait is bounded by a globaltimer deadline; a wait that runs out sets
 // status[0] = 1 and the whole grid winds down (the producer first waits for its
 // copies in flight).
@@ -113,8 +113,8 @@ __device__ uint64_t g_wait_acc[2];  // ns thread 0 of CTAs 0 / 100 spent waiting
   } while (0)
 #endif
 
-// Warp roles: 0..7 compute (digitise, tile-chunk math, attention, embedding), 8 epilogue
-// (sums each tile's chunk results in k-block order, stores, greedy tracking), 9 producer.
+// Warp roles: 0..13 compute (digitise, tile-chunk math, attention, embedding), 14 epilogue
+// (sums each tile's chunk results in k-block order, stores, greedy tracking), 15 producer.
 constexpr int P_EWARP = P_CWARPS, P_PWARP = P_CWARPS + 1;
 constexpr int P_MAXSTAGES = 8, P_STAGE_UNITS = 16, P_RES_STAGES = 8;
 static_assert(P_SLOT_BYTES / 2304 <= P_CWARPS && P_SLOT_BYTES / 2304 <= P_STAGE_UNITS, "a stage holds at most one chunk per compute warp");
@@ -858,7 +858,7 @@ __device__ __forceinline__ void prefetch_l2(const void *src, unsigned bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
-// Producer (lane 0 of warp 9): every weight chunk of this CTA, in execution order,
+// Producer (lane 0 of warp 15): every weight chunk of this CTA, in execution order,
 // into the ring; optionally the same stream a.l2_ahead stages earlier into L2, so
 // HBM keeps streaming while the other warps wait at barriers.
 __device__ void producer(const PersistArgs &a, const Ring &R, volatile int *stop) {
@@ -937,7 +937,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
     return;
   }
 
-  // ---------------- compute warps (0..7) and the epilogue warp (8)
+  // ---------------- compute warps (0..13) and the epilogue warp (14)
   const bool comp = warp < P_CWARPS, epi = warp == P_EWARP;
   const int grid = gridDim.x, c = blockIdx.x;
   unsigned gen = 0;  // grid barriers passed in this launch (thread 0)
@@ -1007,7 +1007,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
         bar_comp();
         if (tid == 0) P_TRACE(step, p, 1);
         const PLane PL = p_lane(lane);
-        // this warp's chunks: u0 + warp, u0 + warp + 8, ... (tile t, super-block kb)
+        // this warp's chunks: u0 + warp, u0 + warp + P_CWARPS, ... (tile t, super-block kb)
         int nu = u0 + warp, kb = nkb ? nu % nkb : 0;
         for (int s0 = u0; s0 < u1; s0 += k, g++) {
           const int s1 = min(u1, s0 + k), slot = g % R.ns, rs = g % P_RES_STAGES;
