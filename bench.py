@@ -489,6 +489,8 @@ def main():
         base = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
                 "sample": f"{n} decode steps of the full model from position 0 (float64 oracle decoder, {threads} threads)"}
 
+    if dist:
+        dist.barrier()  # no rank frees its exchange buffers while a peer may still use them
     eng.dispose()
     qwen = None
     if rank == 0 and world == 1:
