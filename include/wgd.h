@@ -130,6 +130,16 @@ WGD_API int wgd_load_weights(wgd_ctx *ctx);
 WGD_API int wgd_model_ready(wgd_ctx *ctx, int *ready);
 /* Resident weight bytes and streamed weight bytes of the placement plan. */
 WGD_API int wgd_model_placement(wgd_ctx *ctx, uint64_t *resident_bytes, uint64_t *streamed_bytes);
+/* The residency rule wgd_model_end applies, as a pure host function (no device
+ * calls): for n matrices of sizes[i] device bytes (whole 256-byte units, in
+ * execution order) placed after `allocated` bytes under `budget`, resident[i]
+ * is 1 for the matrices kept on the device and 0 for those streamed through
+ * the two page slots, whose size goes to *slot_bytes (0 when nothing streams).
+ * Replaces the cache/stream decision of WeightPager (src/core/pager.ts:22,37-41:
+ * a resident prefix while cacheBudget = limit - allocated - 16 MiB allows,
+ * then one streaming slot). */
+WGD_API int wgd_plan_residency(const uint64_t *sizes, int n, uint64_t allocated, uint64_t budget, uint64_t page_bytes,
+                               uint64_t unit_max, int32_t *resident, uint64_t *slot_bytes);
 
 /* One forward over n token ids at positions [start, start+n); replaces
  * PagedEngine.forward (engine.ts:138-180). want: 0 no output, 1 greedy token

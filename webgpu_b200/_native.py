@@ -60,6 +60,8 @@ SIGNATURES = {
     "wgd_load_weights": (c_int, [c_void_p]),
     "wgd_model_ready": (c_int, [c_void_p, ctypes.POINTER(c_int)]),
     "wgd_model_placement": (c_int, [c_void_p, ctypes.POINTER(c_uint64), ctypes.POINTER(c_uint64)]),
+    "wgd_plan_residency": (c_int, [ctypes.POINTER(c_uint64), c_int, c_uint64, c_uint64, c_uint64, c_uint64,
+                                   ctypes.POINTER(c_int32), ctypes.POINTER(c_uint64)]),
     "wgd_forward": (c_int, [c_void_p, ctypes.POINTER(c_int32), c_int, c_int, c_int, ctypes.POINTER(c_int32), ctypes.POINTER(c_float)]),
     "wgd_decode": (c_int, [c_void_p, c_int32, c_int, c_int, ctypes.POINTER(c_int32)]),
     "wgd_forward_sample": (c_int, [c_void_p, ctypes.POINTER(c_int32), c_int, c_int, ctypes.c_double, c_int, ctypes.c_double,

@@ -422,21 +422,56 @@ static int alloc_linear(wgd_ctx *ctx, DevLinear &L, int type, int rows, int cols
   return WGD_OK;
 }
 
-// Places the matrices in execution order: on the device while they fit the budget (less a 16 MiB
-// margin, the cacheBudget rule of pager.ts:22), the rest in pinned host memory mapped into the
-// device address space (repacked there at upload, copied page by page into the slots per forward).
-static int place_matrices(wgd_ctx *ctx) {
+// The residency rule, with no device calls: matrices of `sizes` device bytes (execution order)
+// all stay on the device when they fit the budget beside `allocated`; otherwise two page slots of
+// max(page, largest page unit) bytes are reserved first, and each matrix stays on the device only
+// while it still fits with a 16 MiB margin (the cacheBudget rule of pager.ts:22), the rest streams.
+// Returns whether anything streams; *slot_bytes is the slot size then (else 0).
+static bool plan_residency(const uint64_t *sizes, int n, uint64_t allocated, uint64_t budget, uint64_t page_bytes,
+                           uint64_t unit_max, int32_t *resident, uint64_t *slot_bytes) {
+  const uint64_t margin = 16u << 20;
   uint64_t need = 0;
+  for (int i = 0; i < n; i++) need += sizes[i];
+  const bool paging = allocated + need > budget;
+  *slot_bytes = 0;
+  if (paging) {
+    *slot_bytes = std::max(page_bytes, unit_max);
+    allocated += 2 * (uint64_t)align_up((int64_t)*slot_bytes, 256);  // what ctx_alloc charges for the two slots
+  }
+  for (int i = 0; i < n; i++) {
+    resident[i] = !paging || allocated + sizes[i] + margin <= budget;
+    if (resident[i]) allocated += sizes[i];
+  }
+  return paging;
+}
+
+extern "C" int wgd_plan_residency(const uint64_t *sizes, int n, uint64_t allocated, uint64_t budget, uint64_t page_bytes,
+                                  uint64_t unit_max, int32_t *resident, uint64_t *slot_bytes) {
+  if ((!sizes || !resident) && n > 0) return fail(WGD_EINVAL, "null argument");
+  if (!slot_bytes || n < 0) return fail(WGD_EINVAL, "bad argument");
+  for (int i = 0; i < n; i++)
+    if (sizes[i] % 256) return fail(WGD_EINVAL, "matrix sizes are whole 256-byte allocation units");
+  plan_residency(sizes, n, allocated, budget, page_bytes, unit_max, resident, slot_bytes);
+  return WGD_OK;
+}
+
+// Places the matrices in execution order by plan_residency: on the device, or in pinned host memory
+// mapped into the device address space (repacked there at upload, copied page by page into the
+// slots per forward).
+static int place_matrices(wgd_ctx *ctx) {
+  std::vector<uint64_t> sizes;
   int64_t unit_max = 0;
   for (DevLinear *L : ctx->pending) {
-    need += (uint64_t)align_up(L->bytes() + 16, 256);
+    sizes.push_back((uint64_t)align_up(L->bytes() + 16, 256));
     unit_max = std::max(unit_max, L->unit_bytes());
   }
-  const uint64_t margin = 16u << 20;
-  ctx->paging = ctx->allocated + need > ctx->budget;
+  std::vector<int32_t> on_device(sizes.size());
+  uint64_t slot_bytes = 0;
+  ctx->paging = plan_residency(sizes.data(), (int)sizes.size(), ctx->allocated, ctx->budget, ctx->page_bytes,
+                               (uint64_t)unit_max, on_device.data(), &slot_bytes);
   int rc;
   if (ctx->paging) {
-    ctx->slot_bytes = std::max<size_t>(ctx->page_bytes, (size_t)unit_max);
+    ctx->slot_bytes = (size_t)slot_bytes;
     for (int i = 0; i < 2; i++)
       if ((rc = ctx_alloc_t(ctx, &ctx->slot[i], ctx->slot_bytes, "page slot"))) return rc;
     CK(cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking));
@@ -448,9 +483,10 @@ static int place_matrices(wgd_ctx *ctx) {
     ctx->st.page_bytes = ctx->slot_bytes;
   }
   uint64_t resident = 0;
-  for (DevLinear *L : ctx->pending) {
-    const uint64_t size = (uint64_t)align_up(L->bytes() + 16, 256);
-    if (!ctx->paging || ctx->allocated + size + margin <= ctx->budget) {
+  for (size_t i = 0; i < ctx->pending.size(); i++) {
+    DevLinear *L = ctx->pending[i];
+    const uint64_t size = sizes[i];
+    if (on_device[i]) {
       if ((rc = ctx_alloc_t(ctx, &L->w, (size_t)size, L->label))) return rc;
       resident += size;
     } else {
