@@ -126,12 +126,18 @@ class WebGPU:
             raise AbortError(err)
         raise RuntimeError(err)
 
+    def _settle(self, result):
+        # sdk.ts:48: a request still pending when the runtime is disposed fails with this message
+        if self._disposed:
+            raise RuntimeError("Runtime disposed.")
+        if result.get("type") == "error":
+            self._raise(result)
+
     def load(self, source, options: dict | None = None):
         _, done, result, listener = self._request("load", {"source": source, "options": options or {}})
         done.wait()
         self._finish(listener)
-        if result["type"] == "error":
-            self._raise(result)
+        self._settle(result)
         return result.get("value")
 
     def generate(self, messages=None, options: dict | None = None, ids=None):
@@ -155,8 +161,7 @@ class WebGPU:
                 self.stop()
                 done.wait()
             self._finish(listener)
-        if result.get("type") == "error":
-            self._raise(result)
+        self._settle(result)
 
     def stop(self):
         """sdk.ts:46 — cancel the running request (worker.ts:8)."""
@@ -170,12 +175,14 @@ class WebGPU:
         _, done, result, listener = self._request("reset", {})
         done.wait()
         self._finish(listener)
-        if result["type"] == "error":
-            self._raise(result)
+        self._settle(result)
 
     def dispose(self):
-        """sdk.ts:48 — ends the worker and frees the device."""
+        """sdk.ts:48 — ends the worker and frees the device; a pending request is cancelled and
+        fails with "Runtime disposed."."""
         self._disposed = True
+        if self._busy:
+            self.stop()
         self._worker.inbox.put(None)
         self._worker.join(timeout=60)
         self._busy = False
