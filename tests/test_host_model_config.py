@@ -2,6 +2,7 @@
 (dense cases) and tests/gguf.test.ts of the reference."""
 import struct
 
+import numpy as np
 import pytest
 
 from webgpu_b200.gguf import GGUF, Tensor, model_config, parse_gguf_header, peek_gguf_header
@@ -113,6 +114,22 @@ def test_peek_reports_architecture_name_quantization():
     p = peek_gguf_header(header([("general.architecture", 8, "llama"), ("general.name", 8, "Llama 3.2 1B Instruct"),
                                  ("general.file_type", 4, 15)]))
     assert p == {"architecture": "llama", "name": "Llama 3.2 1B Instruct", "quantization": "Q4_K_M"}
+
+
+def test_peek_reads_a_small_model_header_through_the_byte_source(tmp_path):
+    from webgpu_b200.gguf import peek_gguf
+    from webgpu_b200.source import MemorySource, make_source
+    data = header([("general.architecture", 8, "qwen3"), ("general.name", 8, "Qwen3 0.6B"), ("general.file_type", 4, 18)])
+    p = tmp_path / "qwen3.gguf"
+    p.write_bytes(data)
+    peek = peek_gguf(make_source(str(p)))
+    assert peek["architecture"] == "qwen3" and peek["quantization"] == "Q6_K"
+    # a header longer than the first 128 KiB read is found by growing the read
+    big = header([("general.description", 8, "x" * 300_000), ("general.architecture", 8, "llama"),
+                  ("general.name", 8, "L"), ("general.file_type", 4, 15)])
+    assert peek_gguf(MemorySource(np.frombuffer(big, np.uint8)))["quantization"] == "Q4_K_M"
+    with pytest.raises(ValueError, match="truncated or invalid"):
+        peek_gguf(MemorySource(np.frombuffer(big[:200_000], np.uint8)))
 
 
 def test_peek_needs_more_bytes_when_truncated():

@@ -369,6 +369,19 @@ def peek_gguf_header(data):
         return None
 
 
+def peek_gguf(source) -> dict:
+    """gguf.ts:242-248 — reads the header through a byte source, doubling the read from 128 KiB
+    until the architecture, name and quantization label parse (8 MiB at most)."""
+    n = min(source.size, 128 * 1024)
+    while True:
+        peek = peek_gguf_header(bytes(source.read(0, n)))
+        if peek:
+            return peek
+        if n >= source.size or n >= 8 * 1024 ** 2:
+            raise ValueError("The GGUF header is truncated or invalid.")
+        n = min(source.size, n * 2)
+
+
 def to_native_config(c: ModelConfig):
     """ModelConfig -> wgd_model_config."""
     from ._native import ModelConfigC
