@@ -88,7 +88,7 @@ class UrlSource(ByteSource):
         self.url = url
         self.size = size
         self.name = name or "local-model.gguf"
-        self._open = opener or (lambda req: urllib.request.urlopen(req))
+        self._open = opener or (lambda req: urllib.request.urlopen(req, timeout=120))  # a stalled server fails the read
 
     def read(self, offset: int, length: int):
         _check(offset, length, self.size)
