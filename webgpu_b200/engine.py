@@ -10,7 +10,7 @@ forward.
 Deliberate differences, for a B200 host: the GPU budget ceiling is the device's
 memory (the reference caps it at a browser's 16 GiB); `LoadOptions` adds
 `tensorParallel`/`rank`/`device`/`exchange` for multi-GPU runs; `generate_ids`
-drives token ids directly (no tokenizer), which the benchmark configurations use.
+drives token ids directly, which the benchmark configurations (no tokenizer metadata) use.
 """
 from __future__ import annotations
 
@@ -26,6 +26,7 @@ from . import _native
 from .context import MAX_CONTEXT, MAX_MESSAGE_CHARS, attention_memory, output_limit, suggest_budget, validate_context
 from .gguf import model_config, read_gguf, to_native_config
 from .source import make_source
+from .tokenizer import make_tokenizer
 
 MiB = 1024 ** 2
 # engine.ts:14-18
@@ -64,54 +65,6 @@ class ModelInfo:
     performance: str
     stats: dict
     tensorParallel: int = 1
-
-
-class ByteTokenizer:
-    """Byte-alphabet chat framing of the reference's dense check models
-    (scripts/verify-dense.mjs:54-58,212-220): token id = UTF-8 byte, plus
-    <|im_start|>/<|im_end|> specials. Full BPE tokenizers are host code the
-    reference keeps unchanged; they are not part of this runtime."""
-
-    def __init__(self, metadata: dict):
-        tokens = metadata.get("tokenizer.ggml.tokens") or []
-        self.tokens = tokens
-        self.start = tokens.index("<|im_start|>") if "<|im_start|>" in tokens else None
-        self.end = tokens.index("<|im_end|>") if "<|im_end|>" in tokens else None
-        eos = metadata.get("tokenizer.ggml.eos_token_id")
-        self.eos = {int(eos)} if eos is not None else set()
-        self.alphabet = {ch: i for i, ch in enumerate(tokens[:256])} if len(tokens) >= 256 else {}
-
-    @property
-    def usable(self) -> bool:
-        return self.start is not None and self.end is not None and len(self.alphabet) == 256
-
-    def chat(self, messages) -> list[int]:
-        if not self.usable:
-            raise ValueError("This model's tokenizer is not available in this host; use generate_ids.")
-        ids: list[int] = []
-        for m in messages:
-            ids += [self.start, *f"{m['role']}\n".encode(), *m["content"].strip().encode(), self.end, *b"\n"]
-        ids += [self.start, *b"assistant\n"]
-        return ids
-
-    def decode(self, ids) -> str:
-        inv = {i: ch for ch, i in self.alphabet.items()}
-        rev = {}
-        # GPT-2 byte alphabet back to bytes
-        kept = [b for b in range(256) if 33 <= b <= 126 or 161 <= b <= 172 or b >= 174]
-        extra = 256
-        for b in range(256):
-            if b in kept:
-                rev[chr(b)] = b
-            else:
-                rev[chr(extra)] = b
-                extra += 1
-        out = bytearray()
-        for i in ids:
-            ch = inv.get(i)
-            if ch is not None and ch in rev:
-                out.append(rev[ch])
-        return out.decode("utf-8", errors="replace")
 
 
 def sample(logits, temperature: float, top_k: int, top_p: float, rng=random.random) -> int:
@@ -179,7 +132,7 @@ class PagedEngine:
         self.budget = b if b is not None else suggest_budget(self.source.size, self.performance)
         if not isinstance(self.budget, int) or self.budget < 512 or self.budget > MAX_BUDGET_MIB:
             raise ValueError(f"GPU budget must be 512–{MAX_BUDGET_MIB} MiB.")
-        self.tokenizer = ByteTokenizer(self.gguf.metadata)
+        self.tokenizer = make_tokenizer(self.gguf.metadata, c.family)
         memory = attention_memory(c, self.context, self.batch)
         self.kv_capacities = memory["capacities"]
         kv_per_rank = memory["total_bytes"] // self.tp
