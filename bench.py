@@ -26,6 +26,9 @@ batches of 128 (untimed), then decode steps from position 512.
          (device time) and wgd_forward_sample per token (wall clock).
   cpu_baseline  the CPU restatement of the reference decoder (oracle/, float64)
          on a bounded sample of the same model, rank 0 only.
+  qwen2_5_0_5b  the benchmark's Qwen2.5-0.5B configuration (23-token prompt, then
+         128 greedy tokens of the device decode loop) with its own roofline
+         fraction, one GPU only; reported beside the headline metric.
 
 --impl reference times that CPU path (the reference's own implementation is
 TypeScript/WebGPU, which has neither a runtime nor a graphics stack here) on
