@@ -14,7 +14,7 @@
  *     failure on the calling thread is wgd_last_error().
  *   - Host buffers are borrowed for the duration of a call. Device memory is
  *     owned by the context and counted against its byte budget, with the same
- *     meaning as the reference's GPU budget (gpu.ts:309-315).
+ *     meaning as the reference's GPU budget (gpu.ts:10,23-30).
  *   - One calling thread per context; wgd_cancel() is the only call that is safe
  *     from another thread.
  *   - The wgd_op_* entry points run one kernel on caller-owned DEVICE pointers
@@ -41,7 +41,7 @@ extern "C" {
 enum wgd_status {
   WGD_OK = 0,
   WGD_EINVAL = 1,       /* bad argument or unsupported shape */
-  WGD_EBUDGET = 2,      /* device budget exceeded (gpu.ts:311) */
+  WGD_EBUDGET = 2,      /* device budget exceeded (gpu.ts:25) */
   WGD_ECUDA = 3,        /* CUDA runtime or kernel error */
   WGD_ECANCELLED = 4,   /* wgd_cancel() observed (engine.ts:128,147 AbortSignal checks) */
   WGD_ETIMEOUT = 5,     /* a bounded wait on a tensor-parallel peer gave up */
@@ -50,20 +50,20 @@ enum wgd_status {
   WGD_EIO = 8           /* the page reader callback failed */
 };
 
-/* GGML tensor types the reference decodes (gguf.ts:43-48). */
+/* GGML tensor types the reference decodes (QUANTS, gguf.ts:6-11; decodeWeight, quant.ts:6-29). */
 enum wgd_ggml_type { WGD_F32 = 0, WGD_F16 = 1, WGD_Q4_0 = 2, WGD_Q8_0 = 8, WGD_Q4_K = 12, WGD_Q5_K = 13, WGD_Q6_K = 14 };
 
-/* Decoder configuration; mirrors ModelConfig (src/core/gguf.ts:124-144) as
- * produced by modelConfig (gguf.ts:145-250). */
+/* Decoder configuration; mirrors ModelConfig (src/core/gguf.ts:87-107) as
+ * produced by modelConfig (gguf.ts:108-213). */
 typedef struct wgd_model_config {
   int32_t family;          /* 0: dense llama/qwen2/qwen3/mistral block, 1: gemma3 block */
   int32_t hidden, intermediate, layers, heads, kv_heads, head_dim, vocab;
   float epsilon, theta, local_theta;
-  int32_t window, period;  /* gemma3 local window and layer period (gguf.ts:168,170) */
+  int32_t window, period;  /* gemma3 local window and layer period (gguf.ts:131,133) */
   float attention_scale, rope_scale;
   int32_t rotary_dim;
-  int32_t rope_mode;       /* 0: half-split (neox), 1: adjacent pairs (norm) (gguf.ts:176) */
-  int32_t sliding_window;  /* dense families: 0 = full context (gguf.ts:177) */
+  int32_t rope_mode;       /* 0: half-split (neox), 1: adjacent pairs (norm) (gguf.ts:139) */
+  int32_t sliding_window;  /* dense families: 0 = full context (gguf.ts:140) */
   int32_t qk_norm, ffn_gate, activation; /* activation 0: silu, 1: gelu */
   int32_t bias_q, bias_k, bias_v, bias_output;
 } wgd_model_config;
@@ -89,9 +89,9 @@ WGD_API int wgd_abi_version(void);
 WGD_API const char *wgd_last_error(void);
 WGD_API int wgd_device_count(int *count);
 
-/* Context on one GPU; replaces Compute.init (gpu.ts:296-307) and the budget
- * (gpu.ts:295). tp_rank/tp_size place this process in a tensor-parallel group
- * (one process per GPU); page_bytes is the pager's page size (pager.ts:13-14). */
+/* Context on one GPU; replaces Compute.init (gpu.ts:11-21) and the budget
+ * (gpu.ts:10). tp_rank/tp_size place this process in a tensor-parallel group
+ * (one process per GPU); page_bytes is the pager's page size (pager.ts:15-19). */
 WGD_API wgd_ctx *wgd_create(int device, int tp_rank, int tp_size, uint64_t budget_bytes, uint32_t page_bytes, int *status);
 WGD_API void wgd_destroy(wgd_ctx *ctx);
 
@@ -108,7 +108,7 @@ WGD_API int wgd_tp_set_timeout(wgd_ctx *ctx, uint64_t spin_limit);
  * Order: model_begin, tensor_register for each directory entry, model_end,
  * tensor_upload (or tensor_host / page reader for streamed weights). */
 WGD_API int wgd_model_begin(wgd_ctx *ctx, const wgd_model_config *cfg, int context_len, int max_batch);
-/* One entry of the GGUF tensor directory (Tensor, gguf.ts:41; dims in GGUF order). */
+/* One entry of the GGUF tensor directory (Tensor, gguf.ts:4; dims in GGUF order). */
 WGD_API int wgd_tensor_register(wgd_ctx *ctx, const char *name, int ggml_type, const uint64_t *dims, int nd,
                         uint64_t file_offset, uint64_t bytes, uint64_t row_bytes);
 WGD_API int wgd_model_end(wgd_ctx *ctx);
@@ -135,7 +135,7 @@ WGD_API int wgd_model_placement(wgd_ctx *ctx, uint64_t *resident_bytes, uint64_t
  * execution order) placed after `allocated` bytes under `budget`, resident[i]
  * is 1 for the matrices kept on the device and 0 for those streamed through
  * the two page slots, whose size goes to *slot_bytes (0 when nothing streams).
- * Replaces the cache/stream decision of WeightPager (src/core/pager.ts:22,37-41:
+ * Replaces the cache/stream decision of the WeightPager class (src/core/pager.ts:22,37-41:
  * a resident prefix while cacheBudget = limit - allocated - 16 MiB allows,
  * then one streaming slot). */
 WGD_API int wgd_plan_residency(const uint64_t *sizes, int n, uint64_t allocated, uint64_t budget, uint64_t page_bytes,
@@ -156,7 +156,7 @@ WGD_API int wgd_decode(wgd_ctx *ctx, int32_t first, int start, int steps, int32_
  * logits readback and sample() of PagedEngine.generate (engine.ts:291,305-324): top_k candidates by
  * value (lower index first among equal values), p = exp((v - best) / temperature), the nucleus cut
  * at top_p, draw = uniform * retained mass. `uniform` in [0, 1) takes the place of Math.random().
- * Settings follow GenerationOptions (engine.ts:264): temperature in [0, 2] (0 = greedy), top_k
+ * Settings follow GenerationOptions (engine.ts:21,264): temperature in [0, 2] (0 = greedy), top_k
  * 1..200, top_p in (0, 1]; otherwise WGD_EINVAL "Invalid sampling settings.". No finite logit:
  * WGD_ENONFINITE. Under tensor parallelism every rank draws the same token (the logits are gathered). */
 WGD_API int wgd_forward_sample(wgd_ctx *ctx, const int32_t *ids, int n, int start, double temperature, int top_k, double top_p,
@@ -198,10 +198,10 @@ WGD_API int wgd_op_sample(const float *logits, int n, double temperature, int to
 WGD_API int64_t wgd_dev_row_bytes(int ggml_type, int64_t cols);
 /* GGUF rows (raw bytes, row stride gguf row bytes) -> device layout rows. */
 WGD_API int wgd_op_repack(int ggml_type, int64_t rows, int64_t cols, const void *raw_dev, void *packed_dev, void *stream);
-/* Bit-exact dequant (WGSL f32 expression order, shaders.ts:42-67) of packed rows. */
+/* Bit-exact dequant (WGSL f32 expression order, weightFunction, shaders.ts:13-38) of packed rows. */
 WGD_API int wgd_op_dequant(int ggml_type, int64_t rows, int64_t cols, const void *packed_dev, float *out_dev, void *stream);
 /* y[b*rows + r] = sum_c W[r][c] * x[b*cols + c] for b < batch (matmulShader,
- * shaders.ts:68-83; expectation verify.ts:32-35). */
+ * shaders.ts:39-54; expectation verify.ts:32-35). */
 WGD_API int wgd_op_gemv(int ggml_type, int64_t rows, int64_t cols, const void *packed_dev, const float *x_dev, int batch,
                 float *y_dev, void *stream);
 /* Tile-16 layout used by the tensor-core GEMV for Q4_K / Q6_K matrices (rows
@@ -217,8 +217,10 @@ WGD_API int wgd_op_gemv_tiled(int ggml_type, int64_t rows, int64_t cols, const v
 /* wgd_op_gemv_tiled for callers that may not allocate device memory while running (no counterpart in
  * the reference, whose WebGPU path has no such constraint): the scratch is a fixed per-device array of
  * 4 MiB of partial sums and 8192 tile counters, and shapes needing more fail with WGD_EINVAL. The first
- * call on a device (that device current) sets the scratch up and should come before any stream capture;
- * later calls allocate nothing. Calls on one device must not overlap in time: they share the scratch. */
+ * call on a device (that device current) looks the scratch up and should come before any stream capture;
+ * no call allocates. The looked-up address is kept for the life of the process, so the device's CUDA
+ * context must not be reset in between. Calls on one device must not overlap in time: they share the
+ * scratch. */
 WGD_API int wgd_op_gemv_tiled_noalloc(int ggml_type, int64_t rows, int64_t cols, const void *tiled_dev, const float *x_dev,
                                       int batch, float *y_dev, void *stream);
 /* Prompt-batch product over tiled Q4_K / Q6_K weights on the tcgen05 tensor cores (the matmul shader,
@@ -230,15 +232,15 @@ WGD_API int wgd_op_gemv_tiled_noalloc(int ggml_type, int64_t rows, int64_t cols,
 WGD_API int wgd_op_gemm_tiled(int ggml_type, int64_t rows, int64_t cols, const void *tiled_dev, const float *x_dev, int batch,
                               float *y_dev, void *stream);
 WGD_API int wgd_op_gemm_tiled_status(int *status);
-/* RMSNorm of n rows (normShader, shaders.ts:84-97). */
+/* RMSNorm of n rows (normShader, shaders.ts:55-68). */
 WGD_API int wgd_op_rmsnorm(const float *x_dev, const float *w_dev, int cols, int n, float eps, float *y_dev, void *stream);
 /* Q/K rotation (+ optional per-head RMS norm) of x[n][heads][hd] in place:
- * ropeShader / ropeNeoxShader / ropeClassicShader (shaders.ts:98-116,167-197).
+ * ropeShader / ropeNeoxShader / ropeClassicShader (shaders.ts:69-87,139-154,155-169).
  * mode 0 half-split, 1 adjacent; norm_w non-null selects the Q/K-norm form. */
 WGD_API int wgd_op_rope(float *x_dev, const float *norm_w_dev, int n, int heads, int hd, int start, float theta, float scale,
                 float eps, int rotary_dim, int mode, void *stream);
 /* Causal GQA attention over a ring cache laid out [kv_heads][capacity][hd]
- * (attentionShader, shaders.ts:117-150). q/out are [n][heads][hd]. */
+ * (attentionShader, shaders.ts:88-122). q/out are [n][heads][hd]. */
 WGD_API int wgd_op_attention(const float *q_dev, const float *k_dev, const float *v_dev, float *out_dev, int n, int heads,
                      int kv_heads, int hd, int start, float scale, int window, int capacity, void *stream);
 /* First finite maximum of x[0..n) (engine.ts:305-309); *idx_dev = -1 when none. */

@@ -8,17 +8,17 @@
  *
  * What it follows (paths inside the reference project, ahpah-dev/WebGPU 0.9.0):
  *   - halfToFloat / decodeWeight          src/core/quant.ts:2-29   (f64, exactly as written)
- *   - fp32 dequant twin in WGSL order     src/core/shaders.ts:44-63 (weightFunction)
+ *   - fp32 dequant twin in WGSL order     src/core/shaders.ts:13-38 (weightFunction)
  *   - packed matmul expectation           src/verify.ts:32-35
  *   - greedy sample                       src/core/engine.ts:305-309
- *   - temperature / top-k / top-p sample  src/core/engine.ts:310-323
+ *   - temperature / top-k / top-p sample  src/core/engine.ts:305-324 (the branch at 310-323)
  *   - RMSNorm / RoPE / attention fixtures src/verify.ts:39-66, src/verify-context.ts:8-41,
- *                                         src/core/shaders.ts:84-150,167-197
+ *                                         src/core/shaders.ts:55-122,139-169
  *   - the float64 CPU decoder             scripts/verify-dense.mjs:138-211
  *     extended with the engine's block    src/core/engine.ts:138-180,217-251 (bias, output
  *     rules                               bias, ungated MLP, sliding window, rope scale, partial
  *                                         rotary) and the Gemma block engine.ts:158-174
- *                                         (post norms, GELU-tanh GLU shaders.ts:165,
+ *                                         (post norms, GELU-tanh GLU shaders.ts:136,
  *                                         sqrt(hidden) embedding scale engine.ts:143,
  *                                         local/global theta and window engine.ts:147,161,163).
  *
@@ -295,7 +295,7 @@ int64_t or_sample(const float *logits, int64_t n, double temperature, int top_k,
 
 /* ------------------------------------------------------- primitive references */
 
-/* shaders.ts:84-97 (normShader), in f64: y = x * rsqrt(mean(x^2) + eps) * w per row. */
+/* shaders.ts:55-68 (normShader), in f64: y = x * rsqrt(mean(x^2) + eps) * w per row. */
 void or_rmsnorm(const float *x, const float *w, int64_t n, int64_t rows, double eps, double *y) {
   for (int64_t r = 0; r < rows; r++) {
     double sum = 0;
@@ -306,8 +306,8 @@ void or_rmsnorm(const float *x, const float *w, int64_t n, int64_t rows, double 
 }
 
 /* Rotary embedding on one head vector (f64, in place).
- * mode 0: half-split pairs (i, i+rot/2) — ropeNeoxShader shaders.ts:168-181 / verify-dense rotate 'neox'
- * mode 1: adjacent pairs (2i, 2i+1)   — ropeClassicShader shaders.ts:184-197 / verify-dense rotate 'norm'
+ * mode 0: half-split pairs (i, i+rot/2) — ropeNeoxShader shaders.ts:139-154 / verify-dense rotate 'neox'
+ * mode 1: adjacent pairs (2i, 2i+1)   — ropeClassicShader shaders.ts:155-169 / verify-dense rotate 'norm'
  * angle = pos * scale / theta^(2i/rot), verify-dense.mjs:149-159. */
 static void rotate_head(double *x, int hd, int rot, int mode, double pos, double scale, double theta) {
   if (rot == 0) rot = hd;
@@ -329,7 +329,7 @@ static void rms_head(double *x, const double *w, int hd, double eps) {
 }
 
 /* Rope op reference over x[n][heads][hd] (f32 in, f64 out), position of row t = start + t.
- * qk_norm != 0 follows ropeShader (shaders.ts:98-116): per-head RMS norm with weight w,
+ * qk_norm != 0 follows ropeShader (shaders.ts:69-87): per-head RMS norm with weight w,
  * then half-split rotation of the first rot dims; the tail keeps the normalised value. */
 void or_rope(const float *x, const float *w, int n, int heads, int hd, int start, double theta, double scale,
              double eps, int rot, int mode, int qk_norm, double *y) {
@@ -345,8 +345,8 @@ void or_rope(const float *x, const float *w, int n, int heads, int hd, int start
   free(wd);
 }
 
-/* attentionShader semantics (shaders.ts:117-150; expectation as verify.ts:47-52 and
- * verify-context.ts:169-178): query row t at absolute position start+t attends keys
+/* attentionShader semantics (shaders.ts:88-122; expectation as verify.ts:47-52 and
+ * verify-context.ts:30-41): query row t at absolute position start+t attends keys
  * [end - min(end, window), end), end = start+t+1, read from ring slot (pos % capacity)
  * of a cache laid out [capacity][kv_heads][hd]. f64 softmax. */
 void or_attention(const float *q, const float *k, const float *v, int n, int heads, int kv_heads, int hd,
@@ -383,7 +383,7 @@ typedef struct or_config {
   int32_t family;          /* 0: dense llama/qwen2/qwen3/mistral, 1: gemma3 */
   int32_t hidden, intermediate, layers, heads, kv_heads, head_dim, vocab;
   double epsilon, theta, local_theta;
-  int32_t window, period;  /* Gemma local window and layer period (gguf.ts:168,170) */
+  int32_t window, period;  /* Gemma local window and layer period (gguf.ts:131,133) */
   double attention_scale, rope_scale;
   int32_t rotary_dim;
   int32_t rope_mode;       /* 0: neox (half split), 1: norm (adjacent pairs) */
@@ -452,6 +452,25 @@ or_state *or_state_create(const or_model *m, int context) {
   for (int l = 0; l < m->c.layers; l++) { s->k[l] = (double *)calloc(per, sizeof(double)); s->v[l] = (double *)calloc(per, sizeof(double)); }
   return s;
 }
+/* Benchmark support, not a parity path: fills the K/V rows of positions [0, n) of every
+ * layer with deterministic values in [-1, 1), so that a decode can start at position n
+ * with the same attention work as after an n-token prompt (the CPU-baseline timing of
+ * decode steps deep in the context). Returns 0, or -1 when n exceeds the context. */
+int or_state_fill(const or_model *m, or_state *s, int n, uint64_t seed) {
+  if (n < 0 || n > s->context) return -1;
+  size_t per = (size_t)n * m->c.kv_heads * m->c.head_dim;
+  for (int l = 0; l < m->c.layers; l++)
+    for (size_t i = 0; i < per; i++) {
+      uint64_t z = seed + 0x9e3779b97f4a7c15ull * (i + 1 + (uint64_t)l * per * 2);
+      z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+      z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+      z ^= z >> 31;
+      s->k[l][i] = (double)(z >> 11) * 0x1.0p-52 - 1.0;
+      s->v[l][i] = (double)((z * 0x2545f4914f6cdd1dull) >> 11) * 0x1.0p-52 - 1.0;
+    }
+  return 0;
+}
+
 void or_state_destroy(or_state *s, const or_model *m) {
   if (!s) return;
   for (int l = 0; l < m->c.layers; l++) { free(s->k[l]); free(s->v[l]); }
@@ -485,7 +504,7 @@ static void project(const double *x, const or_tensor *w, const or_tensor *bias, 
 }
 
 static double silu(double g) { return g / (1.0 + exp(-g)); }
-/* shaders.ts:165 */
+/* shaders.ts:136 */
 static double gelu_tanh(double x) { return 0.5 * x * (1.0 + tanh(0.7978845608 * (x + 0.044715 * x * x * x))); }
 
 /* One decoder step per token, as verify-dense.mjs:165-211 does; prefill batches

@@ -162,7 +162,7 @@ def test_graph_replay_equals_eager(cuda):
 
 def test_budget_and_argument_errors(cuda):
     """Weights beyond the budget are paged (test_gpu_pager); what must fit is the attention state
-    (checked by the host, gpu.ts:309-315 wording) and the fixed device buffers (checked by the
+    (checked by the host, engine.ts:72 wording) and the fixed device buffers (checked by the
     library: WGD_EBUDGET from model_end)."""
     import ctypes
 

@@ -2,7 +2,7 @@
 oracle. Mirrors the reference's per-kernel GPU checks (src/verify.ts:12-74 and
 src/verify-context.ts:7-45 of ahpah-dev/WebGPU 0.9.0) with their fixtures and
 their tolerance: |got - expected| <= 1e-3 * max(1, |expected|) (verify.ts:11),
-abs 1e-3 for long-context attention (verify-context.ts:177). Dequantised
+abs 1e-3 for long-context attention (verify-context.ts:39). Dequantised
 weights must be bit-exact with the WGSL-order fp32 oracle."""
 import math
 

@@ -21,7 +21,7 @@ STATUS_NAMES = {0: "OK", 1: "EINVAL", 2: "EBUDGET", 3: "ECUDA", 4: "ECANCELLED",
 
 
 class ModelConfigC(ctypes.Structure):
-    """wgd_model_config (mirrors ModelConfig, gguf.ts:124-144 of the reference)."""
+    """wgd_model_config (mirrors ModelConfig, gguf.ts:87-107 of the reference)."""
     _fields_ = [("family", c_int32), ("hidden", c_int32), ("intermediate", c_int32), ("layers", c_int32),
                 ("heads", c_int32), ("kv_heads", c_int32), ("head_dim", c_int32), ("vocab", c_int32),
                 ("epsilon", c_float), ("theta", c_float), ("local_theta", c_float), ("window", c_int32),

@@ -325,7 +325,7 @@ int wgd_model_begin(wgd_ctx *ctx, const wgd_model_config *cfg, int context_len, 
   if (!ctx || !cfg) return fail(WGD_EINVAL, "null argument");
   if (ctx->begun) return fail(WGD_ESTATE, "model already configured");
   const wgd_model_config &c = *cfg;
-  // ModelConfig validation (gguf.ts:186) plus what the kernels need.
+  // ModelConfig validation (gguf.ts:149) plus what the kernels need.
   if (c.layers < 1 || c.hidden < 1 || c.heads < 1 || c.head_dim < 1 || c.kv_heads < 1 || c.intermediate < 1 ||
       c.vocab < 1 || c.heads % c.kv_heads || c.head_dim % 2 || c.rotary_dim % 2 || c.rotary_dim > c.head_dim ||
       c.layers > 128 || c.heads > 256 || c.head_dim > 512 || c.hidden > 16384 || c.intermediate > 131072 || c.vocab > 1000000)
@@ -696,7 +696,7 @@ extern "C" int wgd_model_end(wgd_ctx *ctx) {
   const int qd = c.heads * hd, kvd = c.kv_heads * hd;
   int rc;
 
-  // ---- directory validation (modelConfig shape checks, gguf.ts:196-249)
+  // ---- directory validation (modelConfig shape checks, gguf.ts:158-212)
   TensorRec *embd, *onorm, *output;
   if ((rc = expect(ctx, "token_embd.weight", H, c.vocab, &embd))) return rc;
   if ((rc = expect(ctx, "output_norm.weight", H, 1, &onorm))) return rc;

@@ -1,6 +1,6 @@
 // Fused dequant GEMV for decode (batch <= 4 per pass), one instantiation set per
 // GGML type (gemv_<type>.cu). Replaces the reference's matmulShader
-// (shaders.ts:68-83 of the reference project: 64 threads per output row,
+// (shaders.ts:39-54 of the reference project: 64 threads per output row,
 // byte-wise loads, one dispatch per weight page).
 //
 // Layout of work:
@@ -46,7 +46,7 @@ struct TReduce {
 };
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
-// shaders.ts:165 of the reference: 0.5*x*(1+tanh(0.7978845608*(x+0.044715*x^3)))
+// shaders.ts:136 of the reference: 0.5*x*(1+tanh(0.7978845608*(x+0.044715*x^3)))
 __device__ __forceinline__ float gelu_tanh_f(float x) {
   return 0.5f * x * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
 }

@@ -1,7 +1,7 @@
 // Block codecs for the device row layouts (see common.cuh: dev_row_bytes).
 //
 // Two views of every GGML type the reference decodes (quant.ts:6-29 and the
-// WGSL weightFunction, shaders.ts:42-67 of the reference project):
+// WGSL weightFunction, shaders.ts:13-38 of the reference project):
 //
 //  * dequant_elem<T>: one value, bit-exact with the WGSL f32 expression order
 //    (each product and difference rounded separately, no FMA contraction).

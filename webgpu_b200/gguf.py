@@ -11,7 +11,7 @@ import math
 import struct
 from dataclasses import dataclass, field
 
-# gguf.ts:43-48
+# gguf.ts:6-11
 QUANTS = {
     0: ("F32", 1, 4), 1: ("F16", 1, 2), 2: ("Q4_0", 32, 18), 8: ("Q8_0", 32, 34),
     12: ("Q4_K", 256, 144), 13: ("Q5_K", 256, 176), 14: ("Q6_K", 256, 210),
@@ -20,12 +20,12 @@ MAX_SAFE_INTEGER = 2 ** 53 - 1
 
 
 class NeedMore(Exception):
-    """The header continues past the bytes read so far (gguf.ts:49)."""
+    """The header continues past the bytes read so far (gguf.ts:12)."""
 
 
 @dataclass
 class Tensor:
-    """gguf.ts:41 — dims in GGUF order (dims[0] is the row width)."""
+    """gguf.ts:4 — dims in GGUF order (dims[0] is the row width)."""
     name: str
     dims: list
     type: int
@@ -43,7 +43,7 @@ class GGUF:
 
 
 class _Reader:
-    """gguf.ts:50-84."""
+    """gguf.ts:13-47."""
 
     def __init__(self, data: bytes | memoryview):
         self.b = memoryview(data)
@@ -101,7 +101,7 @@ class _Reader:
 
 
 def parse_gguf_header(data, file_size: int) -> GGUF:
-    """gguf.ts:85-114."""
+    """gguf.ts:48-77."""
     r = _Reader(data)
     if r.u32() != 0x46554747:
         raise ValueError("Select a GGUF model file.")
@@ -144,7 +144,7 @@ def parse_gguf_header(data, file_size: int) -> GGUF:
 
 
 def read_gguf(source) -> GGUF:
-    """gguf.ts:115-120 — grow the header read from 4 MiB until it parses (64 MiB cap)."""
+    """gguf.ts:78-83 — grow the header read from 4 MiB until it parses (64 MiB cap)."""
     n = min(source.size, 4 * 1024 ** 2)
     while True:
         try:
@@ -160,7 +160,7 @@ DENSE = {"llama", "qwen2", "qwen3"}
 
 @dataclass
 class ModelConfig:
-    """gguf.ts:124-144."""
+    """gguf.ts:87-107."""
     architecture: str
     family: str
     hidden: int
@@ -198,7 +198,7 @@ def _js_number(v):
 
 
 def model_config(g: GGUF) -> ModelConfig:
-    """gguf.ts:145-250 (the qwen35 hybrid family is recognised and rejected here:
+    """gguf.ts:108-213 (the qwen35 hybrid family is recognised and rejected here:
     its recurrent blocks are outside this runtime's decoder)."""
     raw = g.metadata.get("general.architecture")
     if not isinstance(raw, str) or not raw:
@@ -323,13 +323,13 @@ def model_config(g: GGUF) -> ModelConfig:
     return cfg
 
 
-# gguf.ts:252-256
+# gguf.ts:222-241
 FILE_TYPES = {0: "F32", 1: "F16", 2: "Q4_0", 3: "Q4_1", 7: "Q8_0", 8: "Q5_0", 9: "Q5_1", 10: "Q2_K", 11: "Q3_K_S",
               12: "Q3_K_M", 13: "Q3_K_L", 14: "Q4_K_S", 15: "Q4_K_M", 16: "Q5_K_S", 17: "Q5_K_M", 18: "Q6_K", 19: "Q8_K"}
 
 
 def peek_gguf_header(data):
-    """gguf.ts:259-278 — architecture, name and quantization label, or None if more bytes are needed."""
+    """gguf.ts:242-248 — architecture, name and quantization label, or None if more bytes are needed."""
     try:
         r = _Reader(data)
         if r.u32() != 0x46554747:

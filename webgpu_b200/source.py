@@ -27,7 +27,7 @@ class ByteSource:
 
 
 def _check(offset: int, length: int, size: int) -> None:
-    # source.ts:59-60
+    # source.ts:17-18
     if offset < 0 or length < 1 or offset + length > size or length > MAX_READ:
         raise ValueError("Invalid model byte range (maximum read: 64 MiB).")
 
