@@ -64,6 +64,8 @@ def lib():
         L.or_state_create.restype = vp
         L.or_state_create.argtypes = [vp, ctypes.c_int]
         L.or_state_destroy.argtypes = [vp, vp]
+        L.or_state_fill.restype = ctypes.c_int
+        L.or_state_fill.argtypes = [vp, vp, ctypes.c_int, ctypes.c_uint64]
         L.or_forward.restype = ctypes.c_int
         L.or_forward.argtypes = [vp, vp, vp, ctypes.c_int, ctypes.c_int, vp]
         _lib = L
@@ -173,6 +175,12 @@ class Decoder:
         if lib().or_forward(self.model, self.state, _ptr(arr), n, start, _ptr(logits)) != 0:
             raise ValueError("oracle forward: bad arguments")
         return logits
+
+    def fill_cache(self, n: int, seed: int = 1) -> None:
+        """Benchmark support: K/V rows of positions [0, n) set to seeded values, so that timing
+        can decode at position n without first running an n-token prompt (not for parity)."""
+        if lib().or_state_fill(self.model, self.state, n, seed) != 0:
+            raise ValueError("fill_cache: n exceeds the context")
 
     def greedy_decode(self, prompt, steps: int, batch: int | None = None):
         """Prefill the prompt, then greedy-decode `steps` tokens. Returns (tokens, logits list)."""

@@ -1,15 +1,18 @@
 """The weight pager (WeightPager, pager.ts:7-47): with a GPU budget smaller than the model, the
 matrices that do not fit stay in pinned host memory and stream through two device page slots
 on a copy stream every forward; the embedding table, if it does not fit, is gathered from host
-memory. A paged load must produce the resident load's tokens and logits (the same kernels over
-row ranges), report streamed bytes, and decode the same tokens through the device loop.
+memory. A paged load must produce the float64 oracle's greedy tokens and logits (within 1e-3
+relative), the resident load's tokens (the same kernels over row ranges), report streamed
+bytes, and decode the same tokens through the device loop.
 """
 import ctypes
 
 import numpy as np
 import pytest
 
+import oracle
 from webgpu_b200 import _native, synth
+from webgpu_b200.gguf import model_config, parse_gguf_header
 from webgpu_b200.engine import PagedEngine
 from webgpu_b200.source import MemorySource
 
@@ -69,6 +72,16 @@ def test_paged_load_matches_resident(cuda, make, budget):
     for a, b in zip(logits, ref_logits):
         assert np.max(np.abs(a - b)) <= 1e-4 * np.max(np.abs(b))
     assert dev == toks[1:] == ref_dev
+    # and both against the float64 CPU oracle on the same ids and positions
+    g = parse_gguf_header(image, image.nbytes)
+    dec = oracle.Decoder(image, g, model_config(g), 64, threads=8)
+    try:
+        o_toks, o_logits = dec.greedy_decode(list(spec.prompt), STEPS)
+    finally:
+        dec.close()
+    assert toks == o_toks
+    for a, b in zip(logits, o_logits):
+        assert np.max(np.abs(a - b)) < 1e-3 * np.max(np.abs(b))
 
 
 def test_pull_loading_through_the_page_reader(cuda):

@@ -88,6 +88,12 @@ def test_argument_checks():
         list(e.generate_ids([1], {"temperature": 3}))
     with pytest.raises(ValueError, match="Invalid sampling settings"):
         list(e.generate_ids([1], {"topK": 201}))
+    # Number.isFinite / Number.isInteger accept numbers only: strings and booleans fail the same check
+    for bad in ({"temperature": "0.7"}, {"topP": None}, {"topK": True}, {"topK": 2.5}):
+        with pytest.raises(ValueError, match="Invalid sampling settings"):
+            list(e.generate_ids([1], bad))
+    with pytest.raises(ValueError, match="maxTokens"):
+        list(e.generate_ids([1], {"maxTokens": True}))
     with pytest.raises(ValueError, match="user/assistant"):
         list(e.generate([{"role": "system", "content": "x"}]))
     with pytest.raises(ValueError, match="no tokens"):

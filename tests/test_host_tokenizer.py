@@ -156,3 +156,11 @@ def test_models_without_tokenizer_metadata_are_driven_by_ids():
     assert isinstance(t, NoTokenizer) and not t.usable
     with pytest.raises(ValueError, match="generate_ids"):
         t.chat([{"role": "user", "content": "x"}])
+
+
+def test_qwen35_pattern_keeps_combining_marks_with_their_letter():
+    """gpt2-tokenizer.ts:17: the qwen35 pre-tokenizer counts \\p{M} as a letter, so a decomposed
+    'e' + U+0301 stays one piece where the qwen2 pattern splits the mark off."""
+    text = "cafe\u0301 nai\u0308ve 12"
+    assert pre_tokenizer("qwen35").findall(text) == ["cafe\u0301", " nai\u0308ve", " ", "1", "2"]
+    assert pre_tokenizer("qwen2").findall(text)[:2] == ["cafe", "\u0301"]

@@ -79,3 +79,24 @@ def test_noalloc_rejects_shapes_beyond_its_scratch(cuda):
         _native.check(L.wgd_op_gemv_tiled_noalloc(Q6_K, rows, cols, w.data_ptr(), x.data_ptr(), 1, y.data_ptr(), None))
     with pytest.raises(_native.WgdError, match="bad type"):
         _native.check(L.wgd_op_gemv_tiled_noalloc(Q4_K, 16, 100, w.data_ptr(), x.data_ptr(), 1, y.data_ptr(), None))
+
+
+def test_noalloc_calls_allocate_no_device_memory(cuda):
+    """After the first call on the device, further calls leave the device's free memory and the
+    torch allocator's bytes unchanged: the scratch is the fixed array, never an allocation."""
+    torch = cuda
+    L = _native.lib()
+    rows, cols = 4096, 14336
+    tiled = _tiled(torch, Q4_K, rows, cols, seed=9)
+    x = torch.from_numpy(synth.normal(cols, 23, 5)).cuda()
+    y = torch.empty(rows, device="cuda")
+    _native.check(L.wgd_op_gemv_tiled_noalloc(Q4_K, rows, cols, tiled.data_ptr(), x.data_ptr(), 1, y.data_ptr(), None))
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    torch0 = torch.cuda.memory_allocated()
+    for _ in range(5):
+        _native.check(L.wgd_op_gemv_tiled_noalloc(Q4_K, rows, cols, tiled.data_ptr(), x.data_ptr(), 1, y.data_ptr(), None))
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert torch.cuda.memory_allocated() == torch0

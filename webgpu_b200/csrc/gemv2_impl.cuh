@@ -484,8 +484,12 @@ __global__ void __launch_bounds__(G2_WARPS * 32) gemv2_kernel(const Gemv2Args a)
   typename Ops::Regs ra, rb;
   const uint8_t *wp = a.w + (size_t)u0 * Ops::CB;  // chunk of unit cu
   if (u0 < u1) Ops::load(wp, lane, ra);
-  pdl_launch_dependents();
+  // The dependents are released only after this kernel's own wait: then at most the next
+  // kernel is resident beside this one, and no kernel two launches later can find
+  // residual-stream lines in L1 that this kernel's norm prologue read and that the
+  // next kernel updated.
   pdl_wait();
+  pdl_launch_dependents();
 
   const G2Smem S = g2_carve(smem, NB, a.cols);
   // the zero record read by lanes without a live MMA column (digit-sum entries of

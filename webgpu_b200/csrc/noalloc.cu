@@ -4,11 +4,16 @@
 // not allocate device memory once they are running.
 //
 // The first call on each device (with that device current) looks the array up
-// with cudaGetSymbolAddress, reads the SM count and clears the tile counters on
-// the caller's stream; that first call should come before any stream capture.
-// Every later call allocates nothing. The array is one per device, so calls on
-// the same device must not overlap in time (two streams running this entry
-// point concurrently share the partials and counters and race).
+// with cudaGetSymbolAddress and reads the SM count; that first call should come
+// before any stream capture, and it is the only one that may make the CUDA
+// runtime load the module. Every call allocates nothing. The split-tile
+// counters need no clearing: the array is zero-initialised when the module
+// loads on a device, and every call leaves the counters at zero again. The
+// cached address assumes the CUDA context of the device lives as long as the
+// process (after a cudaDeviceReset it would be stale). The array is one per
+// device, so calls on the same device must not overlap in time (two streams
+// running this entry point concurrently share the partials and counters and
+// race).
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -66,9 +71,6 @@ extern "C" int wgd_op_gemv_tiled_noalloc(int type, int64_t rows, int64_t cols, c
       if ((e = cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
         return cuda_fail("cudaDeviceGetAttribute(SM count)", e);
       unsigned char *b = static_cast<unsigned char *>(base);
-      // the split-tile counters must start at zero; the kernel leaves them zeroed after each call
-      if ((e = cudaMemsetAsync(b + kPartBytes, 0, kTileCounters * sizeof(unsigned), (cudaStream_t)stream)) != cudaSuccess)
-        return cuda_fail("cudaMemsetAsync(tile counters)", e);
       d.part = reinterpret_cast<float *>(b);
       d.ctr = reinterpret_cast<unsigned *>(b + kPartBytes);
       d.sm = sm;

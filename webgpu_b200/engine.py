@@ -36,6 +36,16 @@ PRESETS = {"lite": {"budget": 512, "batch": 8, "page": 16},
 MAX_BUDGET_MIB = 180 * 1024  # one B200's HBM; the browser reference stops at 16384
 
 
+def _is_number(v) -> bool:
+    """A JavaScript number: int or float, but not bool (Number.isFinite(true) is false)."""
+    return isinstance(v, (int, float)) and not isinstance(v, bool)
+
+
+def _is_integer(v) -> bool:
+    """Number.isInteger: an integral number (2.0 counts), never a bool or a string."""
+    return _is_number(v) and math.isfinite(v) and float(v).is_integer()
+
+
 class AbortError(Exception):
     """Raised when a request is cancelled (the reference's AbortError, sdk.ts:27)."""
 
@@ -311,14 +321,16 @@ class PagedEngine:
 
     def _generate(self, prompt, options, signal):
         max_tokens = options.get("maxTokens", 128)
-        if not isinstance(max_tokens, int) or max_tokens < 1 or max_tokens > MAX_CONTEXT:
+        if not _is_integer(max_tokens) or max_tokens < 1 or max_tokens > MAX_CONTEXT:
             raise ValueError(f"maxTokens must be 1–{MAX_CONTEXT}.")
         temperature = options.get("temperature", 0.7)
         top_k = options.get("topK", 40)
         top_p = options.get("topP", 0.9)
-        if (not math.isfinite(temperature) or temperature < 0 or temperature > 2 or not isinstance(top_k, int) or top_k < 1
-                or top_k > 200 or not math.isfinite(top_p) or top_p <= 0 or top_p > 1):
+        if (not _is_number(temperature) or not math.isfinite(temperature) or temperature < 0 or temperature > 2
+                or not _is_integer(top_k) or top_k < 1 or top_k > 200
+                or not _is_number(top_p) or not math.isfinite(top_p) or top_p <= 0 or top_p > 1):
             raise ValueError("Invalid sampling settings.")
+        max_tokens, top_k = int(max_tokens), int(top_k)
         self.busy = True
         try:
             limit = output_limit(max_tokens, len(prompt), self.context)

@@ -52,6 +52,14 @@ def lib():
         L.synth_fill_normal.argtypes = [vp, i64, u64, u64, ctypes.c_double, ctypes.c_double]
         L.synth_fill_ints.restype = None
         L.synth_fill_ints.argtypes = [vp, i64, u64, u64, ctypes.c_int32]
+        L.synth_set_threads.restype = None
+        L.synth_set_threads.argtypes = [ctypes.c_int]
+        # every visible core, also under a launcher that exports OMP_NUM_THREADS=1 (the bytes do
+        # not depend on the thread count)
+        try:
+            L.synth_set_threads(len(os.sched_getaffinity(0)))
+        except AttributeError:
+            L.synth_set_threads(os.cpu_count() or 1)
         _LIB = L
     return _LIB
 

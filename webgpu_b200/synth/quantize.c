@@ -13,8 +13,20 @@
 #include <math.h>
 #include <stdint.h>
 #include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
 
 enum { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14 };
+
+/* Worker threads of the OpenMP loops below (a launcher may have set OMP_NUM_THREADS=1). */
+void synth_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
 
 static inline uint64_t mix64(uint64_t z) {
   z += 0x9e3779b97f4a7c15ull;

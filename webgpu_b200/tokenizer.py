@@ -95,6 +95,9 @@ _PATTERNS = {
     "llama-bpe": _LLAMA3, "llama3": _LLAMA3, "smollm": _LLAMA3, "deepseek-llm": _LLAMA3,
     "qwen2": (rf"(?:{_CONTRACTION})|[^\r\n\p{{L}}\p{{N}}]?\p{{L}}+|\p{{N}}| ?[^\s\p{{L}}\p{{N}}]+[\r\n]*|\s*[\r\n]+"
               r"|\s+(?!\S)|\s+"),
+    # qwen35: combining marks (\p{M}) count as letters, so a base letter and its marks stay one piece
+    "qwen35": (rf"(?:{_CONTRACTION})|[^\r\n\p{{L}}\p{{N}}]?[\p{{L}}\p{{M}}]+|\p{{N}}| ?[^\s\p{{L}}\p{{M}}\p{{N}}]+[\r\n]*"
+               r"|\s*[\r\n]+|\s+(?!\S)|\s+"),
     "gpt2": rf"(?:{_CONTRACTION})| ?\p{{L}}+| ?\p{{N}}+| ?[^\s\p{{L}}\p{{N}}]+|\s+(?!\S)|\s+",
     "default": rf"(?:{_CONTRACTION})| ?\p{{L}}+| ?\p{{N}}+| ?[^\s\p{{L}}\p{{N}}]+|\s+(?!\S)|\s+",
 }
