@@ -169,6 +169,10 @@ struct wgd_ctx {
   std::string persist_why = "not built";
   PersistArgs pargs{};
   int *h_status = nullptr;  // pinned mirror of pargs.status
+  // tensor-parallel persistent launches: arrivals on this rank's cross-rank counter and tokens
+  // decoded so far (identical on every rank of the group); a wait that ran out breaks the group
+  unsigned x_arrivals = 0, x_tokens = 0;
+  bool tp_broken = false;
   // weight pager (WeightPager, pager.ts): matrices that do not fit the budget live in pinned host
   // memory and stream through two device page slots on a copy stream
   std::vector<DevLinear *> pending;  // matrices placed by model_end, in execution order
@@ -528,29 +532,38 @@ static int build_persist_plan(wgd_ctx *ctx) {
   const int H = c.hidden, hd = c.head_dim;
   ctx->persist_ok = false;
   auto no = [&](const char *why) { ctx->persist_why = why; return WGD_OK; };
-  if (ctx->tp_size != 1) return no("tensor-parallel runs use the per-kernel path");
   if (ctx->paging) return no("weights are paged through device slots (per-kernel path)");
+  if (ctx->tp_size > P_TP_MAX) return no("more tensor-parallel ranks than the kernel's exchange holds");
+  if (ctx->tp_size > 1 && ctx->sm_count + 1 > P_CAND_STRIDE) return no("more CTAs than the cross-rank candidate table holds");
   if (c.family == 1) return no("the gemma block (post-norms) uses the per-kernel path");
   const int G = ctx->kv_l ? ctx->heads_l / ctx->kv_l : 0;
-  if (hd % 4 || hd > 256 || G < 1 || G > 8) return no("attention shape outside the persistent kernel");
-  // at least 8 super-blocks per row: the kernel's epilogue warp folds at most two tile ends per ring stage
-  auto tiled_ok = [](const DevLinear &L) { return L.tiled && L.cols % 256 == 0 && L.cols / 256 >= 8; };
+  if (hd % 16 || hd > 128 || G < 1 || G > 8)
+    return no("attention shape outside the persistent kernel (head_dim 16..128 in steps of 16, GQA group <= 8)");
+  auto tiled_ok = [](const DevLinear &L) { return L.tiled && L.cols % 256 == 0 && L.cols >= 256; };
   if (!tiled_ok(ctx->lm)) return no("the LM head is not in the tiled layout");
   int max_cols = H;
   for (auto &L : ctx->layers) {
     if (!tiled_ok(L.qkv) || !tiled_ok(L.o) || !tiled_ok(L.gate_up) || !tiled_ok(L.down))
-      return no("a projection is not in the tiled layout (Q4_K/Q6_K, width >= 2048)");
+      return no("a projection is not in the tiled layout (Q4_K/Q6_K, width a multiple of 256)");
     max_cols = std::max(max_cols, std::max(L.o.cols, L.down.cols));
   }
   if (max_cols > 16384) return no("a projection input is wider than the kernel's digit records");
-  const int ns = persist_max_stages(max_cols, G, hd);
+  const int tpn = ctx->tp_size;
+  // tensor parallelism: the summed input row of a phase (hidden plus the peers' partials) sits in
+  // shared memory behind that phase's digit records
+  const int row_cols = tpn > 1 ? H : 0;
+  const int ns = persist_max_stages(max_cols, G, hd, row_cols);
   if (ns < 3) return no("not enough shared memory for the weight ring");
   int xs = 0;
-  const size_t smem = persist_smem_bytes(max_cols, G, hd, ns, &xs);
+  const size_t smem = persist_smem_bytes(max_cols, G, hd, ns, &xs, row_cols);
   const int grid = ctx->sm_count;
   const bool gemma = false, qkn = c.qk_norm != 0;
   std::vector<PPhase> plan;
-  for (auto &L : ctx->layers) {
+  // residual stream: one buffer at tp = 1 (the O and down epilogues add into it); at tp > 1 two,
+  // alternating between the phases that sum the ranks' partial rows (hb[1] = the projection buffer)
+  float *hb[2] = {ctx->hidden, tpn > 1 ? ctx->proj : ctx->hidden};
+  for (size_t li = 0; li < ctx->layers.size(); li++) {
+    Layer &L = ctx->layers[li];
     auto gemv_phase = [&](const DevLinear &W, const float *x, const float *norm_w, float *y, const float *bias, int epi) {
       PPhase p{};
       p.kind = PH_GEMV;
@@ -568,7 +581,14 @@ static int build_persist_plan(wgd_ctx *ctx) {
       p.g.epi = epi;
       return p;
     };
-    plan.push_back(gemv_phase(L.qkv, ctx->hidden, L.attn_norm, ctx->qkv, L.qkv_bias, EPI_STORE));
+    {
+      PPhase p = gemv_phase(L.qkv, tpn > 1 && li > 0 ? hb[1] : hb[0], L.attn_norm, ctx->qkv, L.qkv_bias, EPI_STORE);
+      if (tpn > 1 && li > 0) {  // hb[1] + the ranks' down partials of the previous layer -> hb[0]
+        p.g.xsum = 2;
+        p.g.x_out = hb[0];
+      }
+      plan.push_back(p);
+    }
     PPhase at{};
     at.kind = PH_ATTN;
     at.a.qkv = ctx->qkv;
@@ -588,10 +608,23 @@ static int build_persist_plan(wgd_ctx *ctx) {
     at.a.scale = c.attention_scale;
     at.a.eps = c.epsilon;
     plan.push_back(at);
-    plan.push_back(gemv_phase(L.o, ctx->att, nullptr, ctx->hidden, L.o_bias, EPI_ADD));
     const int epi = !c.ffn_gate ? EPI_SILU : c.activation == 1 ? EPI_GLU_GELU : EPI_GLU_SILU;
-    plan.push_back(gemv_phase(L.gate_up, ctx->hidden, L.ffn_norm, ctx->act, nullptr, epi));
-    plan.push_back(gemv_phase(L.down, ctx->act, nullptr, ctx->hidden, nullptr, EPI_ADD));
+    if (tpn == 1) {
+      plan.push_back(gemv_phase(L.o, ctx->att, nullptr, ctx->hidden, L.o_bias, EPI_ADD));
+      plan.push_back(gemv_phase(L.gate_up, ctx->hidden, L.ffn_norm, ctx->act, nullptr, epi));
+      plan.push_back(gemv_phase(L.down, ctx->act, nullptr, ctx->hidden, nullptr, EPI_ADD));
+    } else {
+      PPhase o = gemv_phase(L.o, ctx->att, nullptr, nullptr, L.o_bias, EPI_STORE);
+      o.g.push = 1;  // partial rows -> slot 0 of every rank
+      plan.push_back(o);
+      PPhase gu = gemv_phase(L.gate_up, hb[0], L.ffn_norm, ctx->act, nullptr, epi);
+      gu.g.xsum = 1;  // hb[0] + the ranks' O partials -> hb[1]
+      gu.g.x_out = hb[1];
+      plan.push_back(gu);
+      PPhase dn = gemv_phase(L.down, ctx->act, nullptr, nullptr, nullptr, EPI_STORE);
+      dn.g.push = 2;  // partial rows -> slot 1 of every rank
+      plan.push_back(dn);
+    }
   }
   {
     PPhase p{};
@@ -602,7 +635,8 @@ static int build_persist_plan(wgd_ctx *ctx) {
     p.g.cols = H;
     p.g.tiles = (ctx->lm.rows + 15) / 16;
     p.g.nkb = H / 256;
-    p.g.x = ctx->hidden;
+    p.g.x = tpn > 1 ? hb[1] : ctx->hidden;
+    if (tpn > 1) p.g.xsum = 2;  // + the ranks' down partials of the last layer
     p.g.norm_w = ctx->out_norm;
     p.g.eps = c.epsilon;
     p.g.y = ctx->logits;
@@ -623,6 +657,11 @@ static int build_persist_plan(wgd_ctx *ctx) {
       (rc = ctx_alloc_t(ctx, &att_ctr, (size_t)ctx->kv_l, "decode attention counters")) ||
       (rc = ctx_alloc_t(ctx, &cand, (size_t)grid, "decode candidates")) || (rc = ctx_alloc_t(ctx, &bar, 2, "grid barrier")) ||
       (rc = ctx_alloc_t(ctx, &status, 4, "decode status")))
+    return rc;
+  float *lead = nullptr;
+  unsigned *lead_flag = nullptr;
+  if ((rc = ctx_alloc_t(ctx, &lead, (size_t)grid * 16, "decode split-tile pieces")) ||
+      (rc = ctx_alloc_t(ctx, &lead_flag, (size_t)grid, "decode split-tile flags")))
     return rc;
   CK(cudaMemcpy(d_plan, plan.data(), plan.size() * sizeof(PPhase), cudaMemcpyHostToDevice));
   int *d_cancel = nullptr;
@@ -648,6 +687,11 @@ static int build_persist_plan(wgd_ctx *ctx) {
   a.xs_bytes = xs;
   a.nsp_max = nsp_max;
   a.l2_ahead = 0;
+  a.lead = lead;
+  a.lead_flag = lead_flag;
+  a.tp = tpn;
+  a.rank = ctx->tp_rank;
+  a.vocab0 = ctx->vocab0;
   if (const char *v = getenv("WGD_PERSIST_L2_AHEAD")) a.l2_ahead = std::max(0, std::min(64, atoi(v)));  // tuning override
   (void)smem;
   ctx->persist_ok = true;
@@ -657,13 +701,47 @@ static int build_persist_plan(wgd_ctx *ctx) {
 
 // Runs `steps` greedy tokens from (first, start) in one launch; the tokens land in
 // d_tokens and the status words in h_io[IO_STATUS..]. Stream-ordered (no sync).
+// Per-launch state of the persistent kernel: the grid-barrier counter and the split-tile flags
+// start at zero; under tensor parallelism, the peers' exchange buffers and the cross-rank counter
+// base of this launch.
+static int persist_prepare(wgd_ctx *ctx, PersistArgs &a) {
+  CK(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), ctx->stream));  // the arrival counter grows from 0 within a launch
+  CK(cudaMemsetAsync(a.lead_flag, 0, sizeof(unsigned) * ctx->sm_count, ctx->stream));
+  if (ctx->tp_size > 1) {
+    if (ctx->tp_broken)
+      return fail(WGD_ETIMEOUT, "a tensor-parallel peer did not answer within the wait limit earlier; reload the model");
+    TpPersistView v{};
+    std::string err;
+    if (tp_persist_view(ctx->tp, &v, &err)) return fail(WGD_ESTATE, err);
+    for (int j = 0; j < P_TP_MAX; j++) a.xbuf[j] = v.buf[j];
+    a.x_bar = v.bar;
+    a.x_cand = v.cand;
+    a.x_slot = v.slot;
+    a.xbase = ctx->x_arrivals;
+    a.xstep0 = ctx->x_tokens;
+    a.x_limit_ns = ctx->tp_spin_limit ? ctx->tp_spin_limit * 1000ull : 2000000000ull;
+  }
+  return WGD_OK;
+}
+
+// After a persistent launch has completed: the cross-rank barriers it passed (two per layer and
+// one per token), identical on every rank of the group, advance the counter base of the next.
+static void persist_account(wgd_ctx *ctx) {
+  if (ctx->tp_size < 2) return;
+  const unsigned done = (unsigned)ctx->h_io[IO_STATUS + 1];
+  if (ctx->h_io[IO_STATUS] == 1) ctx->tp_broken = true;
+  ctx->x_arrivals += done * (2u * (unsigned)ctx->c.layers + 1u) * (unsigned)(ctx->tp_size * ctx->sm_count);
+  ctx->x_tokens += done;
+}
+
 static int enqueue_persist(wgd_ctx *ctx, int first, int start, int steps) {
   PersistArgs a = ctx->pargs;
   a.first = first;
   a.start = start;
   a.steps = steps;
+  int rc;
   CK(cudaMemsetAsync(a.status, 0, 4 * sizeof(int), ctx->stream));
-  CK(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), ctx->stream));  // the arrival counter grows from 0 within a launch
+  if ((rc = persist_prepare(ctx, a))) return rc;
   CK(launch_persist(a, ctx->sm_count, ctx->stream));
   CK(cudaMemcpyAsync(ctx->h_io + IO_STATUS, a.status, 4 * sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
   ctx->kernels = 1;
@@ -673,6 +751,7 @@ static int enqueue_persist(wgd_ctx *ctx, int first, int start, int steps) {
 
 // Maps the persistent kernel's status word to the API's errors.
 static int persist_status(wgd_ctx *ctx) {
+  persist_account(ctx);
   switch (ctx->h_io[IO_STATUS]) {
     case 0: return WGD_OK;
     case 2: return fail(WGD_ENONFINITE, "Inference produced non-finite logits. Stop and report this model/runtime combination.");
@@ -1314,7 +1393,7 @@ static int forward_impl(wgd_ctx *ctx, const int32_t *ids, int n, int start, int 
   CK(cudaEventRecord(ctx->ev0, ctx->stream));
   int rc;
   const bool gather_logits = want == 2 || (sampled && ctx->tp_size > 1);  // the draw reads the whole row on every rank
-  const bool persist = n == 1 && ctx->persist_ok && ctx->persist_on;
+  const bool persist = n == 1 && ctx->persist_ok && ctx->persist_on && !(ctx->tp_size > 1 && (gather_logits || sampled));
   if (persist) {
     ctx->h_io[IO_CANCEL] = 0;
     if ((rc = enqueue_persist(ctx, ids[0], start, 1))) return rc;
@@ -1475,7 +1554,7 @@ extern "C" int wgd_decode_sample(wgd_ctx *ctx, int32_t first, int start, int ste
   CK(cudaMemcpyAsync(ctx->d_ids, ctx->h_io + 2, sizeof(int32_t), cudaMemcpyHostToDevice, ctx->stream));
   CK(cudaMemcpyAsync(ctx->d_step, ctx->h_io + 3, sizeof(int32_t), cudaMemcpyHostToDevice, ctx->stream));
   CK(cudaMemsetAsync(ctx->d_err, 0, sizeof(int32_t), ctx->stream));
-  const bool persist = ctx->persist_ok && ctx->persist_on;
+  const bool persist = ctx->persist_ok && ctx->persist_on && ctx->tp_size == 1;  // the draw reads every rank's logits
   if (!persist && !ctx->chain_smp_exec && !ctx->paging) {
     CK(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
     rc = enqueue_forward(ctx, 1, ctx->tp_size > 1, false);
@@ -1506,7 +1585,7 @@ extern "C" int wgd_decode_sample(wgd_ctx *ctx, int32_t first, int start, int ste
   CK(cudaEventRecord(ctx->ev0, ctx->stream));
   for (int i = 0; i < steps; i++) {
     if (persist) {
-      CK(cudaMemsetAsync(pa.bar, 0, sizeof(unsigned), ctx->stream));  // arrival counter of this launch
+      if ((rc = persist_prepare(ctx, pa))) return rc;
       CK(launch_persist(pa, ctx->sm_count, ctx->stream));
       ctx->kernels = 1;
       if ((rc = enqueue_sample(ctx, ctx->d_step))) return rc;

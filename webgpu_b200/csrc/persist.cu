@@ -135,11 +135,16 @@ __device__ __forceinline__ void bar_comp() { asm volatile("bar.sync 3, %0;" ::"n
 __device__ __forceinline__ int chunk_bytes(int type) { return type == Q4_K ? 2304 : 3360; }
 __device__ __forceinline__ int slot_units(int type) { return P_SLOT_BYTES / chunk_bytes(type); }
 
-// CTA c owns whole output tiles [tiles*c/grid, tiles*(c+1)/grid): no tile is cut
-// between CTAs (at most one tile of imbalance, no cross-CTA reduction).
+// CTA c owns units [U*c/grid, U*(c+1)/grid) of the phase's U = tiles * nkb units (tile-major, k
+// blocks in order inside a tile): every CTA gets the same number of units to within one. A tile
+// cut between CTAs is finished by the CTA that holds its first unit, which adds the pieces of the
+// following CTAs in k order (the lead sums), so every output has one fixed summation order.
+__device__ __forceinline__ int unit_at(int tiles, int nkb, int grid, int c) {
+  return (int)((long long)tiles * nkb * c / grid);
+}
 __device__ __forceinline__ void unit_range(int tiles, int nkb, int grid, int c, int &u0, int &u1) {
-  u0 = (int)((long long)tiles * c / grid) * nkb;
-  u1 = (int)((long long)tiles * (c + 1) / grid) * nkb;
+  u0 = unit_at(tiles, nkb, grid, c);
+  u1 = unit_at(tiles, nkb, grid, c + 1);
 }
 
 // better(a, b): a is a finite logit with a higher value, or equal value and lower index
@@ -202,6 +207,9 @@ __device__ __forceinline__ PLane p_lane(int lane) {
 // loads: warp w holds super-blocks w, w+16, ... in registers, the norm's sum of
 // squares comes from the same registers. x ~= s * (a + b/254 + c/254^2), s =
 // max|x|/127 per super-block (the same digits as the stand-alone GEMV).
+// SM: x is a row in this CTA's shared memory (the tensor-parallel sum, p_sum_parts), else in global
+// memory (read through L2).
+template <bool SM>
 __device__ void p_digitise(const float *x, const float *nw, float eps, int cols, bool q6, const PX &X, float *red, int *sums,
                            int warp, int lane) {
   const int nsb = cols >> 8;
@@ -214,7 +222,8 @@ __device__ void p_digitise(const float *x, const float *nw, float eps, int cols,
     for (int p = 0; p < 2; p++) {
       const int col = 256 * sb + 32 * ((lane >> 3) + 4 * p) + 4 * q8;
       const bool in = sb < nsb;
-      v[i][p] = in ? __ldcg(reinterpret_cast<const float4 *>(x + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (SM) v[i][p] = in ? *reinterpret_cast<const float4 *>(x + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+      else v[i][p] = in ? __ldcg(reinterpret_cast<const float4 *>(x + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
       // the norm weights are read after the block-wide sum: bring them into L1 now
       if (in && nw) asm volatile("prefetch.global.L1 [%0];" ::"l"(nw + col));
     }
@@ -303,6 +312,25 @@ __device__ void p_digitise(const float *x, const float *nw, float eps, int cols,
     }
     __syncwarp();
   }
+}
+
+// Tensor parallelism: the phase input is x plus the nparts partial rows at part (stride floats
+// apart), added in rank order (the same sum on every CTA of every rank) into the shared-memory row
+// dst; CTA (super-block mod grid) also stores its super-blocks of the sum to x_out, the residual
+// stream that later phases read. Compute warps only; ends with their named barrier.
+__device__ void p_sum_parts(const float *x, const float *part, int nparts, int stride, int cols, float *dst, float *x_out) {
+  const int tid = threadIdx.x;
+  for (int c4 = tid; c4 < (cols >> 2); c4 += P_CWARPS * 32) {
+    const int col = 4 * c4;
+    float4 v = __ldcg(reinterpret_cast<const float4 *>(x + col));
+    for (int j = 0; j < nparts; j++) {
+      const float4 w = __ldcg(reinterpret_cast<const float4 *>(part + (size_t)j * stride + col));
+      v = make_float4(v.x + w.x, v.y + w.y, v.z + w.z, v.w + w.w);
+    }
+    *reinterpret_cast<float4 *>(dst + col) = v;
+    if (x_out && (col >> 8) % (int)gridDim.x == (int)blockIdx.x) __stcg(reinterpret_cast<float4 *>(x_out + col), v);
+  }
+  asm volatile("bar.sync 3, %0;" ::"n"(P_CWARPS * 32) : "memory");
 }
 
 // MMA shapes with the operand signedness the chunk math needs (D = A*B, zero C).
@@ -460,8 +488,10 @@ __device__ __forceinline__ void p_q6k(const uint8_t *c, int kb, const PX &X, con
 
 struct GemvCtx {
   const PGemv *g;
+  const PersistArgs *a;
   float best_v;  // greedy tracking (per lane)
   int best_i;
+  int row0;      // global index of output row 0 (the vocabulary offset of this rank's LM head rows)
 };
 
 // Epilogue of one finished tile: lane r < 16 holds the value of tile row r.
@@ -476,6 +506,13 @@ __device__ __forceinline__ void p_epilogue(GemvCtx &C, int t, float v, int lane)
   if (lane < 16 && row < g.rows) {
     float val = v;
     if (g.bias) val += __ldg(g.bias + row);
+    if (g.push) {
+      // this rank's partial row into its slot of every rank's exchange buffer (peer stores over NVLink)
+      const PersistArgs &a = *C.a;
+      const size_t off = ((size_t)(g.push - 1) * P_TP_MAX + a.rank) * a.hidden + row;
+      for (int j = 0; j < a.tp; j++) reinterpret_cast<float *>(a.xbuf[j] + a.x_slot)[off] = val;
+      return;
+    }
     if (g.epi == EPI_ADD) {
       val = __ldcg(g.y + row) + val;
       g.y[row] = val;
@@ -485,11 +522,45 @@ __device__ __forceinline__ void p_epilogue(GemvCtx &C, int t, float v, int lane)
     } else {
       g.y[row] = val;
     }
-    if (g.argmax && isfinite(val) && better(val, row, C.best_v, C.best_i)) {
+    if (g.argmax && isfinite(val) && better(val, C.row0 + row, C.best_v, C.best_i)) {
       C.best_v = val;
-      C.best_i = row;
+      C.best_i = C.row0 + row;
     }
   }
+}
+
+// ------------------------------------------------------------------ split tiles
+
+__device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// The sum of this CTA's first piece of a tile that started in an earlier CTA's range, for
+// the CTA that finishes the tile (epilogue warp; lane r < 16 holds row r).
+__device__ void p_lead_store(const PersistArgs &a, int c, float v, unsigned tag, int lane) {
+  if (lane < 16) __stcg(a.lead + (size_t)c * 16 + lane, v);
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) st_release_gpu(a.lead_flag + c, tag);
+}
+
+// Waits (bounded) until CTA c2 has published its lead piece of phase `tag`; false when the grid
+// is winding down or the wait ran out (then status[0] = 1 and the stop flag is raised).
+__device__ bool p_lead_wait(const unsigned *lead_flag, int *status, int c2, unsigned tag, volatile int *stop);
+
+// The pieces of tile t_end that the CTAs after c computed (in k order), summed; a real call, so
+// that the epilogue warp's stage loop keeps its registers. A wait that runs out raises *stop.
+__device__ __noinline__ float p_fetch_pieces(const float *lead, const unsigned *lead_flag, int *status, int tiles, int nkb, int c,
+                                             int grid, int t_end, unsigned tag, volatile int *stop, int lane) {
+  float sum = 0.f;
+  for (int c2 = c + 1; c2 < grid; c2++) {
+    const int v0 = unit_at(tiles, nkb, grid, c2);
+    if (v0 >= (t_end + 1) * nkb) break;
+    if (unit_at(tiles, nkb, grid, c2 + 1) == v0) continue;  // an empty range holds no piece
+    if (!p_lead_wait(lead_flag, status, c2, tag, stop)) break;  // the stop flag is raised
+    sum += __ldcg(lead + (size_t)c2 * 16 + (lane & 15));
+  }
+  return sum;
 }
 
 // ------------------------------------------------------------------ attention item
@@ -531,203 +602,248 @@ __device__ __forceinline__ void attn_split(const PAttn &A, int pos, int nspmax, 
   nsp = (L + chunk - 1) / chunk;
 }
 
-// One (kv head, key split) of decode attention by consumer warps 0..3 (128 threads,
-// named barrier 2). `staged`: stage 0 already holds the first K/V tile (issued while
-// the QKV projection ran).
+// One (kv head, key split) of decode attention. Every compute warp enters; warps 0..3 (named
+// barrier 2) stage K/V, rotate q/k and run the tiles, and all 14 merge the key splits of the kv head
+// when this CTA is the last to finish one (named barrier 3). Per 32-key tile:
+//   scores   warp w sums dims [w*hd/4, (w+1)*hd/4) for every query head of the group, lane = key
+//            (each K row is read once for all heads), the four parts added in warp order;
+//   softmax  warp w owns heads w, w+4: running max / sum per head (shared memory), the tile's
+//            probabilities to shared memory;
+//   P.V      warp w takes keys j = w (mod 4), lane = four dims, every head at once (each V row read
+//            once), its partial sums rescaled by the heads' corrections; the four warps' sums are
+//            added in warp order at the end.
+// `staged`: stage 0 already holds the first K/V tile (issued while the QKV projection ran).
+constexpr int AW = 4;  // warps of the tile work
+__device__ __forceinline__ float *attn_scratch(float *sm, int G, int hd) { return sm + 2 * attn_stage_floats(hd) + G * hd + 2 * hd; }
+
 __device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, int chunk, int nspmax, float *sm, float *att_part,
-                            unsigned *att_ctr, int *last_s, bool staged) {
+                            unsigned *att_ctr, int *last_s, bool staged, int tr_step, int tr_phase) {
+  (void)tr_step;
+  (void)tr_phase;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = A.heads / A.kv_heads, hd = A.hd, hd4 = hd >> 2, RS = hd + 4;
   float *q_s = sm + 2 * attn_stage_floats(hd), *kn_s = q_s + G * hd, *vn_s = kn_s + hd;
+  float *sc_s = attn_scratch(sm, G, hd);  // [AW][8][32] score parts
+  float *pr_s = sc_s + AW * 8 * 32;       // [32][8] probabilities of the tile
+  float *st_s = pr_s + 32 * 8;            // [3][8] running max, running sum, correction
   const int end = pos + 1, begin = end - (end < A.window ? end : A.window);
   const int p0 = begin + sp * chunk, p1 = min(end, p0 + chunk);
   const bool owns_new = p1 == end;
   const int ntiles = (p1 - p0 + 31) / 32;
-  if (!staged) p_attn_stage(A, pos, kh, p1, p0, sm, 0, tid);
-  if (ntiles > 1) p_attn_stage(A, pos, kh, p1, p0 + 32, sm, 1, tid);
-  const int hq = G + (owns_new ? 1 : 0);
-  // this lane's RoPE (cos, sin) pairs, requested together with q/k/v (the same for every head)
-  const int half = A.rot / 2;
-  const float2 *tb = A.table + (int64_t)pos * half;
-  float2 cs[4];
+  const int PR = hd + 4;
+  float *out_base = A.out + (int64_t)kh * G * hd;
+  if (warp < AW) {
+    if (!staged) p_attn_stage(A, pos, kh, p1, p0, sm, 0, tid);
+    if (ntiles > 1) p_attn_stage(A, pos, kh, p1, p0 + 32, sm, 1, tid);
+    const int hq = G + (owns_new ? 1 : 0);
+    // this lane's RoPE (cos, sin) pairs, requested together with q/k/v (the same for every head)
+    const int half = A.rot / 2;
+    const float2 *tb = A.table + (int64_t)pos * half;
+    float2 cs[4];
 #pragma unroll
-  for (int k = 0; k < 4; k++) cs[k] = lane + 32 * k < half ? __ldg(tb + lane + 32 * k) : make_float2(1.f, 0.f);
-  for (int i = tid; i < hq * hd; i += 128) {
-    const int g = i / hd, d = i - g * hd;
-    const float *src = g < G ? A.qkv + (int64_t)(kh * G + g) * hd : A.qkv + (int64_t)(A.heads + kh) * hd;
-    (g < G ? q_s + g * hd : kn_s)[d] = __ldcg(src + d);
-  }
-  if (owns_new)
-    for (int d = tid; d < hd; d += 128) vn_s[d] = __ldcg(A.qkv + (int64_t)(A.heads + A.kv_heads + kh) * hd + d);
-  asyncb();
-  for (int g = warp; g < hq; g += 4) {
-    float *hv = g < G ? q_s + g * hd : kn_s;
-    const float *nw = g < G ? A.q_norm : A.k_norm;
-    if (nw) {
-      float ss = 0.f;
-      for (int d = lane; d < hd; d += 32) ss = fmaf(hv[d], hv[d], ss);
-      const float inv = rsqrtf(warp_sum(ss) / (float)hd + A.eps);
-      __syncwarp();
-      for (int d = lane; d < hd; d += 32) hv[d] = hv[d] * inv * nw[d];
-      __syncwarp();
+    for (int k = 0; k < 4; k++) cs[k] = lane + 32 * k < half ? __ldg(tb + lane + 32 * k) : make_float2(1.f, 0.f);
+    for (int i = tid; i < hq * hd; i += AW * 32) {
+      const int g = i / hd, d = i - g * hd;
+      const float *src = g < G ? A.qkv + (int64_t)(kh * G + g) * hd : A.qkv + (int64_t)(A.heads + kh) * hd;
+      (g < G ? q_s + g * hd : kn_s)[d] = __ldcg(src + d);
     }
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const int i = lane + 32 * k;
-      if (i >= half) break;
-      const int ia = A.mode == 0 ? i : 2 * i, ib = A.mode == 0 ? i + half : 2 * i + 1;
-      const float l = hv[ia], r = hv[ib];
-      hv[ia] = l * cs[k].x - r * cs[k].y;
-      hv[ib] = l * cs[k].y + r * cs[k].x;
+    if (owns_new)
+      for (int d = tid; d < hd; d += AW * 32) vn_s[d] = __ldcg(A.qkv + (int64_t)(A.heads + A.kv_heads + kh) * hd + d);
+    if (tid < 8) {
+      st_s[tid] = -FLT_MAX;
+      st_s[8 + tid] = 0.f;
     }
-    __syncwarp();
-  }
-  asyncb();
-  if (owns_new) {
-    const int slot = pos % A.capacity;
-    float *kd = A.k + ((int64_t)kh * A.capacity + slot) * hd, *vd = A.v + ((int64_t)kh * A.capacity + slot) * hd;
-    for (int d = tid; d < hd; d += 128) { kd[d] = kn_s[d]; vd[d] = vn_s[d]; }
-  }
-  const int g0 = warp, g1 = warp + 4;
-  const bool h0 = g0 < G, h1 = g1 < G;
-  float m0 = -FLT_MAX, m1 = -FLT_MAX, l0 = 0.f, l1 = 0.f;
-  float4 acc0[2], acc1[2];
-#pragma unroll
-  for (int i = 0; i < 2; i++) acc0[i] = acc1[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int ti = 0; ti < ntiles; ti++) {
-    const int tile = p0 + ti * 32, cnt = min(32, p1 - tile), st = ti & 1;
-    if (ti + 1 < ntiles) cp_wait<1>(); else cp_wait<0>();
     asyncb();
-    float *ks = attn_stage(sm, hd, st), *vs = ks + 32 * RS;
-    if (owns_new && tile + cnt == end) {
-      const int r = end - 1 - tile;
-      for (int d = tid; d < hd; d += 128) { ks[r * RS + d] = kn_s[d]; vs[r * RS + d] = vn_s[d]; }
-      asyncb();
-    }
-    const bool live = lane < cnt;
-    float s0 = 0.f, s1 = 0.f;
-    {
-      const float4 *kr = reinterpret_cast<const float4 *>(ks + lane * RS);
-      const float4 *q0 = reinterpret_cast<const float4 *>(q_s + g0 * hd);
-      const float4 *q1 = reinterpret_cast<const float4 *>(q_s + (h1 ? g1 : g0) * hd);
-#pragma unroll 8
-      for (int d4 = 0; d4 < hd4; d4++) {
-        const float4 k4 = kr[d4];
-        if (h0) {
-          const float4 q = q0[d4];
-          s0 = fmaf(q.x, k4.x, fmaf(q.y, k4.y, fmaf(q.z, k4.z, fmaf(q.w, k4.w, s0))));
-        }
-        if (h1) {
-          const float4 q = q1[d4];
-          s1 = fmaf(q.x, k4.x, fmaf(q.y, k4.y, fmaf(q.z, k4.z, fmaf(q.w, k4.w, s1))));
-        }
+    for (int g = warp; g < hq; g += AW) {
+      float *hv = g < G ? q_s + g * hd : kn_s;
+      const float *nw = g < G ? A.q_norm : A.k_norm;
+      if (nw) {
+        float ss = 0.f;
+        for (int d = lane; d < hd; d += 32) ss = fmaf(hv[d], hv[d], ss);
+        const float inv = rsqrtf(warp_sum(ss) / (float)hd + A.eps);
+        __syncwarp();
+        for (int d = lane; d < hd; d += 32) hv[d] = hv[d] * inv * nw[d];
+        __syncwarp();
       }
-    }
-    float e0 = 0.f, e1 = 0.f;
-    if (h0) {
-      s0 = live ? s0 * A.scale : -FLT_MAX;
-      const float mn = fmaxf(m0, warp_max(s0)), corr = expf(m0 - mn);
-      e0 = live ? expf(s0 - mn) : 0.f;
-      l0 = fmaf(l0, corr, warp_sum(e0));
-      m0 = mn;
 #pragma unroll
-      for (int i = 0; i < 2; i++) acc0[i] = make_float4(acc0[i].x * corr, acc0[i].y * corr, acc0[i].z * corr, acc0[i].w * corr);
+      for (int k = 0; k < 4; k++) {
+        const int i = lane + 32 * k;
+        if (i >= half) break;
+        const int ia = A.mode == 0 ? i : 2 * i, ib = A.mode == 0 ? i + half : 2 * i + 1;
+        const float l = hv[ia], r = hv[ib];
+        hv[ia] = l * cs[k].x - r * cs[k].y;
+        hv[ib] = l * cs[k].y + r * cs[k].x;
+      }
+      __syncwarp();
     }
-    if (h1) {
-      s1 = live ? s1 * A.scale : -FLT_MAX;
-      const float mn = fmaxf(m1, warp_max(s1)), corr = expf(m1 - mn);
-      e1 = live ? expf(s1 - mn) : 0.f;
-      l1 = fmaf(l1, corr, warp_sum(e1));
-      m1 = mn;
-#pragma unroll
-      for (int i = 0; i < 2; i++) acc1[i] = make_float4(acc1[i].x * corr, acc1[i].y * corr, acc1[i].z * corr, acc1[i].w * corr);
+    asyncb();
+    if (tid == 0) P_TRACE(tr_step, tr_phase, 1);
+    if (owns_new) {
+      const int slot = pos % A.capacity;
+      float *kd = A.k + ((int64_t)kh * A.capacity + slot) * hd, *vd = A.v + ((int64_t)kh * A.capacity + slot) * hd;
+      for (int d = tid; d < hd; d += AW * 32) { kd[d] = kn_s[d]; vd[d] = vn_s[d]; }
     }
-    if (h0) {
-#pragma unroll 4
-      for (int j = 0; j < cnt; j++) {
-        const float w0 = __shfl_sync(0xffffffffu, e0, j), w1 = __shfl_sync(0xffffffffu, e1, j);
-        const float4 *vr = reinterpret_cast<const float4 *>(vs + j * RS);
+    const int dq = hd >> 4;  // float4s of the score dims of one warp
+    float4 acc[8];
 #pragma unroll
-        for (int i = 0; i < 2; i++) {
-          const int d4 = lane + 32 * i;
-          if (d4 < hd4) {
-            const float4 v = vr[d4];
-            acc0[i] = make_float4(fmaf(w0, v.x, acc0[i].x), fmaf(w0, v.y, acc0[i].y), fmaf(w0, v.z, acc0[i].z), fmaf(w0, v.w, acc0[i].w));
-            if (h1)
-              acc1[i] = make_float4(fmaf(w1, v.x, acc1[i].x), fmaf(w1, v.y, acc1[i].y), fmaf(w1, v.z, acc1[i].z), fmaf(w1, v.w, acc1[i].w));
+    for (int g = 0; g < 8; g++) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int ti = 0; ti < ntiles; ti++) {
+      const int tile = p0 + ti * 32, cnt = min(32, p1 - tile), st = ti & 1;
+      if (ti + 1 < ntiles) cp_wait<1>(); else cp_wait<0>();
+      asyncb();
+      float *ks = attn_stage(sm, hd, st), *vs = ks + 32 * RS;
+      if (owns_new && tile + cnt == end) {
+        const int r = end - 1 - tile;
+        for (int d = tid; d < hd; d += AW * 32) { ks[r * RS + d] = kn_s[d]; vs[r * RS + d] = vn_s[d]; }
+        asyncb();
+      }
+      {  // scores: this warp's quarter of the dims, every head, lane = key
+        const float4 *kr = reinterpret_cast<const float4 *>(ks + lane * RS) + warp * dq;
+        float sp2[8][2];
+#pragma unroll
+        for (int g = 0; g < 8; g++) sp2[g][0] = sp2[g][1] = 0.f;
+        for (int i = 0; i < dq; i++) {
+          const float4 k4 = kr[i];
+#pragma unroll
+          for (int g = 0; g < 8; g++) {
+            if (g < G) {
+              const float4 q = reinterpret_cast<const float4 *>(q_s + g * hd)[warp * dq + i];
+              sp2[g][0] = fmaf(q.x, k4.x, fmaf(q.y, k4.y, sp2[g][0]));
+              sp2[g][1] = fmaf(q.z, k4.z, fmaf(q.w, k4.w, sp2[g][1]));
+            }
           }
         }
+#pragma unroll
+        for (int g = 0; g < 8; g++)
+          if (g < G) sc_s[(warp * 8 + g) * 32 + lane] = sp2[g][0] + sp2[g][1];
       }
-    }
-    asyncb();
-    if (ti + 2 < ntiles) p_attn_stage(A, pos, kh, p1, tile + 64, sm, st, tid);
-  }
-  float *out_base = A.out + (int64_t)kh * G * hd;
-  if (nsp == 1) {
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
-      const int d4 = lane + 32 * i;
-      if (d4 < hd4) {
-        if (h0) reinterpret_cast<float4 *>(out_base + g0 * hd)[d4] = make_float4(acc0[i].x / l0, acc0[i].y / l0, acc0[i].z / l0, acc0[i].w / l0);
-        if (h1) reinterpret_cast<float4 *>(out_base + g1 * hd)[d4] = make_float4(acc1[i].x / l1, acc1[i].y / l1, acc1[i].z / l1, acc1[i].w / l1);
-      }
-    }
-    return;
-  }
-  const int PR = hd + 4;
-  float *part = att_part + ((int64_t)kh * nspmax + sp) * G * PR;
-#pragma unroll
-  for (int i = 0; i < 2; i++) {
-    const int d4 = lane + 32 * i;
-    if (d4 < hd4) {
-      if (h0) __stcg(reinterpret_cast<float4 *>(part + g0 * PR) + d4, acc0[i]);
-      if (h1) __stcg(reinterpret_cast<float4 *>(part + g1 * PR) + d4, acc1[i]);
-    }
-  }
-  if (lane == 0) {
-    if (h0) { __stcg(part + g0 * PR + hd, m0); __stcg(part + g0 * PR + hd + 1, l0); }
-    if (h1) { __stcg(part + g1 * PR + hd, m1); __stcg(part + g1 * PR + hd + 1, l1); }
-  }
-  __threadfence();
-  asyncb();
-  if (tid == 0) *last_s = atomicAdd(att_ctr + kh, 1u) == (unsigned)(nsp - 1);
-  asyncb();
-  if (!*last_s) return;
-  __threadfence();
-  const float *pb = att_part + (int64_t)kh * nspmax * G * PR;
-  const int64_t sstride = (int64_t)G * PR;
-  for (int g = warp; g < G; g += 4) {
-    const float *ph = pb + g * PR;
-    // the first batch of partial vectors goes out with the (m, l) loads: one round trip for both
-    const float ma = lane < nsp ? __ldcg(ph + lane * sstride + hd) : -FLT_MAX;
-    const float mb = lane + 32 < nsp ? __ldcg(ph + (lane + 32) * sstride + hd) : -FLT_MAX;
-    const float M = warp_max(fmaxf(ma, mb));
-    const float wa = lane < nsp ? expf(ma - M) : 0.f, wb = lane + 32 < nsp ? expf(mb - M) : 0.f;
-    const float la = lane < nsp ? __ldcg(ph + lane * sstride + hd + 1) : 0.f;
-    const float lb = lane + 32 < nsp ? __ldcg(ph + (lane + 32) * sstride + hd + 1) : 0.f;
-    const float den = warp_sum(fmaf(wa, la, wb * lb));
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
-      const int d4 = lane + 32 * i;
-      float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
-      // the split partials in batches of 8 independent loads (one L2 round trip per batch)
-      for (int j0 = 0; j0 < nsp; j0 += 8) {
-        float4 pv[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++)
-          pv[u] = j0 + u < nsp && d4 < hd4 ? __ldcg(reinterpret_cast<const float4 *>(ph + (j0 + u) * sstride) + d4)
-                                             : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-          const int j = j0 + u;  // splits past nsp have weight 0 and a zero partial
-          const float w = __shfl_sync(0xffffffffu, j < 32 ? wa : wb, j & 31);
-          num = make_float4(fmaf(w, pv[u].x, num.x), fmaf(w, pv[u].y, num.y), fmaf(w, pv[u].z, num.z), fmaf(w, pv[u].w, num.w));
+      asyncb();
+      for (int g = warp; g < G; g += AW) {  // online softmax of head g over this tile
+        float sv = ((sc_s[(0 * 8 + g) * 32 + lane] + sc_s[(1 * 8 + g) * 32 + lane]) + sc_s[(2 * 8 + g) * 32 + lane]) +
+                   sc_s[(3 * 8 + g) * 32 + lane];
+        const bool live = lane < cnt;
+        sv = live ? sv * A.scale : -FLT_MAX;
+        const float mo = st_s[g], mn = fmaxf(mo, warp_max(sv)), corr = expf(mo - mn);
+        const float e = live ? expf(sv - mn) : 0.f;
+        const float ls = warp_sum(e);
+        pr_s[lane * 8 + g] = e;
+        if (lane == 0) {
+          st_s[g] = mn;
+          st_s[8 + g] = fmaf(st_s[8 + g], corr, ls);
+          st_s[16 + g] = corr;
         }
       }
-      if (d4 < hd4) reinterpret_cast<float4 *>(out_base + g * hd)[d4] = make_float4(num.x / den, num.y / den, num.z / den, num.w / den);
+      asyncb();
+      if (lane < hd4) {  // P.V: keys j = warp (mod 4), four dims per lane, every head
+        float cr[8];
+#pragma unroll
+        for (int g = 0; g < 8; g++) cr[g] = g < G ? st_s[16 + g] : 0.f;
+#pragma unroll
+        for (int g = 0; g < 8; g++) acc[g] = make_float4(acc[g].x * cr[g], acc[g].y * cr[g], acc[g].z * cr[g], acc[g].w * cr[g]);
+        for (int j = warp; j < cnt; j += AW) {
+          const float4 v = reinterpret_cast<const float4 *>(vs + j * RS)[lane];
+          const float4 pa = reinterpret_cast<const float4 *>(pr_s + j * 8)[0], pb = reinterpret_cast<const float4 *>(pr_s + j * 8)[1];
+          const float pw[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+          for (int g = 0; g < 8; g++)
+            if (g < G)
+              acc[g] = make_float4(fmaf(pw[g], v.x, acc[g].x), fmaf(pw[g], v.y, acc[g].y), fmaf(pw[g], v.z, acc[g].z),
+                                   fmaf(pw[g], v.w, acc[g].w));
+        }
+      }
+      asyncb();
+      if (ti + 2 < ntiles) p_attn_stage(A, pos, kh, p1, tile + 64, sm, st, tid);
     }
+    if (tid == 0) P_TRACE(tr_step, tr_phase, 2);
+    // the four warps' P.V sums, added in warp order (stage 1 is free now: no copy is in flight)
+    float4 *cb = reinterpret_cast<float4 *>(sm);  // [AW][G][hd4]
+    if (lane < hd4) {
+#pragma unroll
+      for (int g = 0; g < 8; g++)
+        if (g < G) cb[(warp * G + g) * hd4 + lane] = acc[g];
+    }
+    asyncb();
+    for (int i = tid; i < G * hd4; i += AW * 32) {
+      const int g = i / hd4, d4 = i - g * hd4;
+      float4 t = cb[g * hd4 + d4];
+#pragma unroll
+      for (int w = 1; w < AW; w++) {
+        const float4 u = cb[(w * G + g) * hd4 + d4];
+        t = make_float4(t.x + u.x, t.y + u.y, t.z + u.z, t.w + u.w);
+      }
+      if (nsp == 1) {
+        const float l = st_s[8 + g];
+        reinterpret_cast<float4 *>(out_base + g * hd)[d4] = make_float4(t.x / l, t.y / l, t.z / l, t.w / l);
+      } else {
+        float *part = att_part + ((int64_t)kh * nspmax + sp) * G * PR;
+        __stcg(reinterpret_cast<float4 *>(part + g * PR) + d4, t);
+        if (d4 == 0) {
+          __stcg(part + g * PR + hd, st_s[g]);
+          __stcg(part + g * PR + hd + 1, st_s[8 + g]);
+        }
+      }
+    }
+    if (nsp > 1) __threadfence();
+    asyncb();
+    if (tid == 0 && nsp > 1) *last_s = atomicAdd(att_ctr + kh, 1u) == (unsigned)(nsp - 1);
+    if (tid == 0) P_TRACE(tr_step, tr_phase, 4);
+  }
+  if (nsp == 1) return;
+  bar_comp();  // every compute warp learns whether this CTA merges the kv head's splits
+  if (!*last_s) return;
+  __threadfence();
+  // merge of the nsp splits by the 14 compute warps: warp g < G turns head g's (max, sum) pairs
+  // into weights; then (output float4, split group) items sum their splits' partials
+  const float *pb = att_part + (int64_t)kh * nspmax * G * PR;
+  const int64_t sstride = (int64_t)G * PR;
+  float *wt_s = attn_scratch(sm, G, hd);  // [8][64] weights (the score scratch is free now)
+  if (warp < G) {
+    const float *ph = pb + warp * PR;
+    const float ma = lane < nsp ? __ldcg(ph + lane * sstride + hd) : -FLT_MAX;
+    const float mb = lane + 32 < nsp ? __ldcg(ph + (lane + 32) * sstride + hd) : -FLT_MAX;
+    const float la = lane < nsp ? __ldcg(ph + lane * sstride + hd + 1) : 0.f;
+    const float lb = lane + 32 < nsp ? __ldcg(ph + (lane + 32) * sstride + hd + 1) : 0.f;
+    const float M = warp_max(fmaxf(ma, mb));
+    const float wa = lane < nsp ? expf(ma - M) : 0.f, wb = lane + 32 < nsp ? expf(mb - M) : 0.f;
+    const float den = warp_sum(fmaf(wa, la, wb * lb));
+    wt_s[warp * 64 + lane] = wa / den;
+    wt_s[warp * 64 + lane + 32] = wb / den;
+  }
+  bar_comp();
+  const int W4 = G * hd4, NG = max(1, min(8, (P_CWARPS * 32) / W4));
+  float4 *cb = reinterpret_cast<float4 *>(sm);  // [NG][W4] group sums
+  if (tid < NG * W4) {
+    const int item = tid % W4, grp = tid / W4, g = item / hd4, d4 = item - g * hd4;
+    const float *ph = pb + g * PR;
+    float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j0 = grp; j0 < nsp; j0 += 8 * NG) {
+      float4 pv[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int j = j0 + u * NG;
+        pv[u] = j < nsp ? __ldcg(reinterpret_cast<const float4 *>(ph + j * sstride) + d4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int j = j0 + u * NG;
+        const float w = j < nsp ? wt_s[g * 64 + j] : 0.f;
+        num = make_float4(fmaf(w, pv[u].x, num.x), fmaf(w, pv[u].y, num.y), fmaf(w, pv[u].z, num.z), fmaf(w, pv[u].w, num.w));
+      }
+    }
+    cb[grp * W4 + item] = num;
+  }
+  bar_comp();
+  for (int i = tid; i < W4; i += P_CWARPS * 32) {
+    const int g = i / hd4, d4 = i - g * hd4;
+    float4 t = cb[i];
+    for (int q = 1; q < NG; q++) {
+      const float4 u = cb[q * W4 + i];
+      t = make_float4(t.x + u.x, t.y + u.y, t.z + u.z, t.w + u.w);
+    }
+    reinterpret_cast<float4 *>(out_base + g * hd)[d4] = t;
   }
   if (tid == 0) att_ctr[kh] = 0u;
+  if (tid == 0) P_TRACE(tr_step, tr_phase, 5);
 }
 
 // ------------------------------------------------------------------ embedding
@@ -783,6 +899,52 @@ __device__ bool mbar_wait(uint64_t *b, unsigned par, volatile int *stop, int *st
     }
   }
   return true;
+}
+
+__device__ bool p_lead_wait(const unsigned *lead_flag, int *status, int c2, unsigned tag, volatile int *stop) {
+  const uint64_t t0 = gtime();
+  for (unsigned it = 1; (int)(ld_acquire(lead_flag + c2) - tag) < 0; it++) {
+    if ((it & 63) == 0) {
+      if (*stop) return false;
+      if (gtime() - t0 > P_TIMEOUT_NS) {
+        atomicCAS(status, 0, 1);
+        *stop = 1;
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// Barrier over every CTA of every rank of a tensor-parallel group, after this CTA's partial rows
+// were pushed to the peers: each CTA adds 1 to the arrival counter in every rank's exchange
+// buffer (system-scope release, after a system-scope fence), then polls its own rank's counter
+// until all tp * grid arrivals of this barrier are in. The counter only grows (across launches
+// too: xbase is the count before this launch), so no reset races a faster peer.
+__device__ bool x_sync(const PersistArgs &a, unsigned &xgen, volatile int *stop) {
+  bar_all();
+  if (threadIdx.x == 0 && !*stop) {
+    __threadfence_system();
+    for (int j = 0; j < a.tp; j++)
+      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.xbuf[j] + a.x_bar) : "memory");
+    const unsigned target = a.xbase + (xgen + 1u) * (unsigned)(gridDim.x * a.tp);
+    const unsigned *ctr = reinterpret_cast<const unsigned *>(a.xbuf[a.rank] + a.x_bar);
+    const uint64_t t0 = gtime();
+    for (unsigned it = 1;; it++) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+      if ((int)(v - target) >= 0) break;
+      if ((it & 63) == 0 && (*(volatile int *)a.status == 1 || gtime() - t0 > a.x_limit_ns)) {
+        atomicCAS(a.status, 0, 1);
+        *stop = 1;
+        break;
+      }
+    }
+    xgen++;
+  }
+  if (threadIdx.x == 0) stop[3] = *stop;
+  bar_all();
+  return !stop[3];
 }
 
 // Grid barrier for the compute and epilogue warps of every CTA. Returns false when
@@ -940,7 +1102,8 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
   // ---------------- compute warps (0..13) and the epilogue warp (14)
   const bool comp = warp < P_CWARPS, epi = warp == P_EWARP;
   const int grid = gridDim.x, c = blockIdx.x;
-  unsigned gen = 0;  // grid barriers passed in this launch (thread 0)
+  unsigned gen = 0;   // grid barriers passed in this launch (thread 0)
+  unsigned xgen = 0;  // cross-rank barriers passed in this launch (thread 0; tensor parallelism)
   unsigned g = 0;  // ring stage counter, in step with the producer
   // the first two phase descriptors; later ones are copied one phase ahead of use
   if (epi) {
@@ -970,10 +1133,10 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
         int chunk, nsp;
         attn_split(A, pos, a.nsp_max, chunk, nsp);
         const int items = A.kv_heads * nsp;
-        if (warp < 4)
+        if (comp)
           for (int it = c; it < items; it += grid)
             p_attn_item(A, pos, it / nsp, it % nsp, nsp, chunk, a.nsp_max, reinterpret_cast<float *>(xs), a.att_part, a.att_ctr,
-                        &sh.flags[1], it == c && att_staged);
+                        &sh.flags[1], it == c && att_staged, step, p);
         att_staged = false;
         if (tid == 0) P_TRACE(step, p, 3);
         alive = grid_sync(a, gen, stop);
@@ -985,11 +1148,28 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
       int u0, u1;
       unit_range(pg.tiles, nkb, grid, c, u0, u1);
       if (comp) {
-        // when attention follows, warps 0..3 start copying this CTA's first K/V tile now
-        // (rows of earlier positions only) into attention stage 0, above the digit records
+        const bool q6 = pg.type == Q6_K;
+        const PX X = px_carve(xs, pg.cols);
+        if (pg.xsum) {
+          // the summed row (residual plus the ranks' partials) sits behind the digit records in xs
+          const float *part = reinterpret_cast<const float *>(a.xbuf[a.rank] + a.x_slot) +
+                              (size_t)(pg.xsum - 1) * P_TP_MAX * a.hidden;
+          float *row = reinterpret_cast<float *>(xs + ((px_bytes(pg.cols) + 15) & ~(size_t)15));
+          p_sum_parts(pg.x, part, a.tp, a.hidden, pg.cols, row, pg.x_out);
+          p_digitise<true>(row, pg.norm_w, pg.eps, pg.cols, q6, X, sh.red, sh.dsum[warp], warp, lane);
+        } else {
+          p_digitise<false>(pg.x, pg.norm_w, pg.eps, pg.cols, q6, X, sh.red, sh.dsum[warp], warp, lane);
+        }
+        bar_comp();
+        if (tid == 0) P_TRACE(step, p, 1);
+        // when attention follows, warps 0..3 start copying this CTA's first K/V tile now (rows
+        // of earlier positions only) into attention stage 0, above the digit records; issued after
+        // the digitisation so that its loads of the phase input do not queue behind these copies
         if (p + 1 < a.nphases && sh.dsc[(q + 1) % 3].kind == PH_ATTN && warp < 4) {
           const PAttn &A = sh.dsc[(q + 1) % 3].a;
-          if (px_bytes(pg.cols) <= (size_t)attn_stage_floats(A.hd) * 4) {
+          // (only where the digit records, and a tensor-parallel input row behind them, end below stage 0)
+          const size_t used = pg.xsum ? ((px_bytes(pg.cols) + 15) & ~(size_t)15) + 4 * (size_t)pg.cols : px_bytes(pg.cols);
+          if (used <= (size_t)attn_stage_floats(A.hd) * 4) {
             int chunk, nsp;
             attn_split(A, pos, a.nsp_max, chunk, nsp);
             if (c < A.kv_heads * nsp) {
@@ -1001,11 +1181,6 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
             }
           }
         }
-        const bool q6 = pg.type == Q6_K;
-        const PX X = px_carve(xs, pg.cols);
-        p_digitise(pg.x, pg.norm_w, pg.eps, pg.cols, q6, X, sh.red, sh.dsum[warp], warp, lane);
-        bar_comp();
-        if (tid == 0) P_TRACE(step, p, 1);
         const PLane PL = p_lane(lane);
         // this warp's chunks: u0 + warp, u0 + warp + P_CWARPS, ... (tile t, super-block kb)
         int nu = u0 + warp, kb = nkb ? nu % nkb : 0;
@@ -1056,39 +1231,88 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
         // epilogue warp: tile sums in k-block order, then the tile's epilogue
         GemvCtx C;
         C.g = &pg;
+        C.a = &a;
         C.best_v = -FLT_MAX;
         C.best_i = -1;
-        int t = nkb ? u0 / nkb : 0, kbe = 0;
+        C.row0 = a.tp > 1 && pg.argmax ? a.vocab0 : 0;
+        int t = nkb ? u0 / nkb : 0, kbe = nkb ? u0 % nkb : 0;
+        const int lead_t = kbe ? t : -1;  // this range starts inside tile t: its piece goes to the tile's owner
+        const unsigned tag = (unsigned)q + 1u;
+        // the range ends inside a tile that starts in it: this CTA owns that tile, and the pieces of
+        // the following CTAs (computed at the start of their ranges) are fetched before the last
+        // stage's results arrive, so the L2 round trips overlap that stage
+        const int t_end = nkb ? u1 / nkb : 0;
+        const bool tail_owner = nkb && u1 > u0 && u1 % nkb != 0 && t_end * nkb >= u0;
+        float pieces = 0.f;
+        bool fetched = false, ok = true;
         float run = 0.f;
+        auto fetch_pieces = [&]() {
+          fetched = true;
+          pieces = p_fetch_pieces(a.lead, a.lead_flag, a.status, pg.tiles, nkb, c, grid, t_end, tag, stop, lane);
+          if (*stop) ok = false;
+        };
+        auto emit = [&](int tt, float vv) {
+          if (tt == lead_t) p_lead_store(a, c, vv, tag, lane);
+          else p_epilogue(C, tt, vv, lane);
+        };
         for (int s0 = u0; s0 < u1; s0 += k, g++) {
           const int n = min(k, u1 - s0), rs = g % P_RES_STAGES;
+          // (not when the last stage is also the first: the following CTA may itself publish its
+          // piece only after its single stage, and a chain of such waits would run serially)
+          if (tail_owner && s0 + k >= u1 && s0 > u0 && ok) fetch_pieces();
           if (mbar_wait(R.done + rs, (g / P_RES_STAGES) & 1u, stop, a.status)) {
             float v[P_STAGE_UNITS];
 #pragma unroll
             for (int j = 0; j < P_STAGE_UNITS; j++) v[j] = (j < n && lane < 16) ? sh.res[rs][j][lane] : 0.f;
             __syncwarp();
             if (lane == 0) mbar_arrive(R.resfree + rs);  // results copied out
-            // the stage's results in k-block order; a tile ends where the running k-block count
-            // reaches nkb. With n <= 16 results and nkb >= 8 (inputs >= 2048 wide) a stage holds at
-            // most two tile ends, so the sums run branch-free and the epilogue is emitted after
-            // the loop (the same additions in the same order as one epilogue per result)
-            const int e1 = nkb - 1 - kbe, e2 = e1 + nkb;
-            float o1 = 0.f, o2 = 0.f;
+            if (nkb >= 8) {
+              // the stage's results in k-block order; a tile ends where the running k-block count
+              // reaches nkb. With n <= 16 results and nkb >= 8 a stage holds at most two tile ends,
+              // so the sums run branch-free and the epilogue is emitted after the loop (the same
+              // additions in the same order as one epilogue per result)
+              const int e1 = nkb - 1 - kbe, e2 = e1 + nkb;
+              float o1 = 0.f, o2 = 0.f;
 #pragma unroll
-            for (int j = 0; j < P_STAGE_UNITS; j++) {
-              if (j < n) {
-                run += v[j];
-                if (j == e1) { o1 = run; run = 0.f; }
-                if (j == e2) { o2 = run; run = 0.f; }
+              for (int j = 0; j < P_STAGE_UNITS; j++) {
+                if (j < n) {
+                  run += v[j];
+                  if (j == e1) { o1 = run; run = 0.f; }
+                  if (j == e2) { o2 = run; run = 0.f; }
+                }
+              }
+              if (e1 < n) emit(t++, o1);
+              if (e2 < n) emit(t++, o2);
+              kbe += n;
+              while (kbe >= nkb) kbe -= nkb;
+            } else {
+              // narrow inputs (tensor-parallel shards): several tile ends per stage
+#pragma unroll
+              for (int j = 0; j < P_STAGE_UNITS; j++) {
+                if (j < n) {
+                  run += v[j];
+                  if (++kbe == nkb) {
+                    emit(t++, run);
+                    run = 0.f;
+                    kbe = 0;
+                  }
+                }
               }
             }
-            if (e1 < n) p_epilogue(C, t++, o1, lane);
-            if (e2 < n) p_epilogue(C, t++, o2, lane);
-            kbe += n;
-            while (kbe >= nkb) kbe -= nkb;
           } else {
+            ok = false;
             __syncwarp();
             if (lane == 0) mbar_arrive(R.resfree + rs);
+          }
+        }
+        // a tile cut at the end of this range: a piece for its owner, or (owner) the tile's end
+        // with the pieces of the following CTAs added
+        if (ok && nkb && kbe != 0 && u1 > u0) {
+          if (t == lead_t) {
+            p_lead_store(a, c, run, tag, lane);
+          } else {
+            if (!fetched) fetch_pieces();
+            if (ok) p_epilogue(C, t, run + pieces, lane);  // own units, then the pieces summed in k order
           }
         }
         if (lane == 0) P_TRACE(step, p, 3);
@@ -1102,20 +1326,41 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
             if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
           }
           if (lane == 0) {
-            __stcg(a.cand + c, make_float2(bv, __int_as_float(bi)));
-            if (c == 0 && a.cancel && *(volatile const int *)a.cancel) atomicExch(a.status + 2, 1);
+            const bool stop_req = c == 0 && a.cancel && *(volatile const int *)a.cancel;
+            if (a.tp > 1) {
+              // every rank's candidate table (two by token parity); rank 0's cancel word rides along
+              // so that every rank stops after the same token
+              const unsigned par = (a.xstep0 + (unsigned)step) & 1u;
+              for (int j = 0; j < a.tp; j++) {
+                float2 *pc = reinterpret_cast<float2 *>(a.xbuf[j] + a.x_cand) + ((size_t)par * P_TP_MAX + a.rank) * P_CAND_STRIDE;
+                pc[c] = make_float2(bv, __int_as_float(bi));
+                if (c == 0 && a.rank == 0) pc[grid] = make_float2(stop_req ? 1.f : 0.f, 0.f);
+              }
+            } else {
+              __stcg(a.cand + c, make_float2(bv, __int_as_float(bi)));
+              if (stop_req) atomicExch(a.status + 2, 1);
+            }
           }
         }
       }
-      alive = grid_sync(a, gen, stop);
+      // after a pushed partial (O, down) or the LM head's candidates, every rank of the group meets
+      alive = a.tp > 1 && (pg.push || pg.argmax) ? x_sync(a, xgen, stop) : grid_sync(a, gen, stop);
     }
     if (!alive) break;
     // greedy token: the best candidate of all CTAs (every CTA computes the same)
     {
       float bv = -FLT_MAX;
       int bi = -1;
-      for (int i = tid; i < grid; i += (P_CWARPS + 1) * 32) {
-        const float2 cv = __ldcg(a.cand + i);
+      const float2 *cand = a.cand;
+      int ncand = grid;
+      if (a.tp > 1) {  // every rank's CTAs, in this rank's buffer
+        cand = reinterpret_cast<const float2 *>(a.xbuf[a.rank] + a.x_cand) +
+               (size_t)((a.xstep0 + (unsigned)step) & 1u) * P_TP_MAX * P_CAND_STRIDE;
+        ncand = a.tp * P_CAND_STRIDE;
+      }
+      for (int i = tid; i < ncand; i += (P_CWARPS + 1) * 32) {
+        if (a.tp > 1 && i % P_CAND_STRIDE >= grid) continue;  // control words and unused slots
+        const float2 cv = __ldcg(cand + i);
         const int ci = __float_as_int(cv.y);
         if (better(cv.x, ci, bv, bi)) { bv = cv.x; bi = ci; }
       }
@@ -1139,7 +1384,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
       }
       bar_all();
       token = sh.flags[2];
-      const bool cancelled = __ldcg(a.status + 2) != 0;
+      const bool cancelled = a.tp > 1 ? __ldcg(cand + grid).x != 0.f : __ldcg(a.status + 2) != 0;
       if (c == 0 && tid == 0) {
         a.tokens[step] = token;
         a.status[1] = step + 1;
@@ -1171,20 +1416,27 @@ extern "C" __attribute__((visibility("default"))) int wgd_debug_persist_bars(uin
 
 // ------------------------------------------------------------------ host side
 
-static int attn_smem_bytes(int group, int hd) { return 4 * (group * hd + 2 * hd + 2 * 2 * 32 * (hd + 4)); }
+static int attn_smem_bytes(int group, int hd) {
+  // K|V stages, q, new k and v rows, score parts [4][8][32], probabilities [32][8], head state [3][8]
+  return 4 * (group * hd + 2 * hd + 2 * 2 * 32 * (hd + 4) + 4 * 8 * 32 + 32 * 8 + 3 * 8);
+}
 
-size_t persist_smem_bytes(int max_cols, int group, int hd, int nstage, int *xs) {
+size_t persist_smem_bytes(int max_cols, int group, int hd, int nstage, int *xs, int row_cols) {
   size_t x = px_bytes(max_cols);
   const size_t at = (size_t)attn_smem_bytes(group, hd);
   if (at > x) x = at;
+  if (row_cols > 0) {
+    const size_t r = ((px_bytes(row_cols) + 15) & ~(size_t)15) + 4 * (size_t)row_cols;
+    if (r > x) x = r;
+  }
   x = (x + 127) & ~(size_t)127;
   if (xs) *xs = (int)x;
   return 256 + (size_t)nstage * P_SLOT_BYTES + x + sizeof(PShared);
 }
 
-int persist_max_stages(int max_cols, int group, int hd) {
+int persist_max_stages(int max_cols, int group, int hd, int row_cols) {
   const size_t limit = 227 * 1024;
-  const size_t fixed = persist_smem_bytes(max_cols, group, hd, 0, nullptr);
+  const size_t fixed = persist_smem_bytes(max_cols, group, hd, 0, nullptr, row_cols);
   if (fixed >= limit) return 0;
   int ns = (int)((limit - fixed) / P_SLOT_BYTES);
   return ns > P_MAXSTAGES ? P_MAXSTAGES : ns;

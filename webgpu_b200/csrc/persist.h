@@ -18,6 +18,7 @@
 namespace wgd {
 
 enum PhaseKind { PH_GEMV = 0, PH_ATTN = 1 };
+constexpr int P_TP_MAX = 8;  // ranks of a tensor-parallel group
 
 struct PGemv {
   const uint8_t *w;  // tiled weights (Q4_K or Q6_K)
@@ -29,6 +30,12 @@ struct PGemv {
   const float *bias;
   int epi;     // Epi
   int argmax;  // track the greedy token over the outputs (LM head)
+  // tensor parallelism: the input is x plus the tp partial rows of exchange slot xsum - 1
+  // (xsum 0: x alone), summed in rank order; the sum is also stored to x_out (super-block sb by
+  // CTA sb % grid) as the residual stream of the next phases. push > 0: the outputs are this
+  // rank's partial rows, stored into slot push - 1 of every rank's exchange buffer.
+  int xsum, push;
+  float *x_out;
 };
 
 struct PAttn {
@@ -70,16 +77,31 @@ struct PersistArgs {
   int *status;          // [0] 0 ok, 1 wait limit hit, 2 non-finite logits, 3 cancelled; [1] steps done
   int nstage, xs_bytes, nsp_max;
   int l2_ahead;  // ring stages requested into L2 ahead of the shared-memory copies (0: none)
+  // split tiles: a CTA's unit range may start inside a tile; the sum of that first piece goes to
+  // lead[c][16] with lead_flag[c] = phase sequence number + 1, and the CTA that holds the start of
+  // the tile adds it (in k order) before the tile's epilogue
+  float *lead;          // [grid][16]
+  unsigned *lead_flag;  // [grid], zero at launch
+  // tensor parallelism (tp > 1): every rank's exchange buffer (own included), mapped here
+  int tp, rank, vocab0;
+  char *xbuf[P_TP_MAX];
+  unsigned long long x_bar, x_cand, x_slot;  // byte offsets of the kernel's region in an exchange buffer
+  unsigned xbase;   // arrivals counted on this rank's cross-rank counter before this launch
+  unsigned xstep0;  // tokens decoded by earlier launches of this group (candidate slot parity)
+  unsigned long long x_limit_ns;  // bound of one cross-rank wait
 };
 
 constexpr int P_CWARPS = 14;                // compute warps (+ one epilogue warp, one producer warp)
+constexpr int P_CAND_STRIDE = 256;          // candidate slots per rank in an exchange buffer (grid + 1 control word)
 constexpr int P_THREADS = (P_CWARPS + 2) * 32;
 constexpr int P_SLOT_BYTES = 32256;        // 14 Q4_K or 9 Q6_K tile chunks
 
 // Shared-memory bytes for a plan whose GEMV inputs are at most max_cols wide and
 // whose attention uses (group, hd); returns the xs region size in *xs.
-size_t persist_smem_bytes(int max_cols, int group, int hd, int nstage, int *xs);
-int persist_max_stages(int max_cols, int group, int hd);
+// row_cols > 0 (tensor parallelism): room for a summed input row of that width behind the digit
+// records of a row_cols-wide phase input.
+size_t persist_smem_bytes(int max_cols, int group, int hd, int nstage, int *xs, int row_cols = 0);
+int persist_max_stages(int max_cols, int group, int hd, int row_cols = 0);
 // Cooperative launch on `grid` CTAs (one per SM).
 cudaError_t launch_persist(const PersistArgs &a, int grid, cudaStream_t s);
 

@@ -28,7 +28,12 @@ struct Header {
 struct Layout {
   size_t flags, aflags, gflags, am, slots, gather, total;
   size_t cap, gcap;
+  size_t pbar, pcand, pslot;  // the persistent kernel's region
 };
+// persistent kernel region: arrival counter (own 256-byte line), candidate tables
+// [2 token parities][TP_MAX ranks][256] (float2), partial-row slots [2][TP_MAX][16384] floats
+// (16384 = the widest hidden size the configuration allows)
+constexpr size_t P_CAND_SLOTS = 256, P_SLOT_FLOATS = 16384;
 static Layout make_layout(size_t cap, size_t gcap) {
   Layout L{};
   size_t o = sizeof(Header);
@@ -40,6 +45,11 @@ static Layout make_layout(size_t cap, size_t gcap) {
   o = (o + 255) / 256 * 256;
   L.slots = o; o += sizeof(float) * 2 * TP_MAX * cap;
   L.gather = o; o += sizeof(float) * gcap;
+  o = (o + 255) / 256 * 256;
+  L.pbar = o; o += 256;
+  L.pcand = o; o += sizeof(float) * 2 * 2 * TP_MAX * P_CAND_SLOTS;
+  o = (o + 255) / 256 * 256;
+  L.pslot = o; o += sizeof(float) * 2 * TP_MAX * P_SLOT_FLOATS;
   L.total = (o + 255) / 256 * 256;
   L.cap = cap;
   L.gcap = gcap;
@@ -268,6 +278,15 @@ __global__ void gather_rows_kernel(const TpDev d, float *rows, int total, unsign
     for (int i = a + threadIdx.x; i < b; i += blockDim.x) rows[i] = __ldcg(g + i);
   }
   finish(d, e);
+}
+
+int tp_persist_view(TpComm *t, TpPersistView *out, std::string *err) {
+  if (!t || !t->opened) return err_out(err, "tensor-parallel peers are not open (call wgd_tp_open_peers)", 6);
+  for (int j = 0; j < TP_MAX; j++) out->buf[j] = j < t->size ? t->peer[j] : nullptr;
+  out->bar = t->L.pbar;
+  out->cand = t->L.pcand;
+  out->slot = t->L.pslot;
+  return 0;
 }
 
 static unsigned long long limit_or_default(unsigned long long l) { return l ? l : (1ull << 25); }

@@ -28,4 +28,13 @@ int tp_argmax_gather(TpComm *t, int *idx, float *val, int vocab0, cudaStream_t s
 int tp_gather_rows(TpComm *t, float *rows, int total, int vocab0, int count, cudaStream_t s, unsigned long long spin_limit,
                    std::string *err);
 
+// The region of the exchange buffers that the persistent decode kernel uses (its own counter,
+// candidate tables and partial-row slots, apart from the exchange kernels' slots and flags):
+// every rank's buffer base as mapped in this process, and the byte offsets inside a buffer.
+struct TpPersistView {
+  char *buf[8];
+  unsigned long long bar, cand, slot;
+};
+int tp_persist_view(TpComm *t, TpPersistView *out, std::string *err);
+
 }  // namespace wgd
