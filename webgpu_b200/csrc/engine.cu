@@ -658,11 +658,7 @@ static int build_persist_plan(wgd_ctx *ctx) {
       (rc = ctx_alloc_t(ctx, &cand, (size_t)grid, "decode candidates")) || (rc = ctx_alloc_t(ctx, &bar, 2, "grid barrier")) ||
       (rc = ctx_alloc_t(ctx, &status, 4, "decode status")))
     return rc;
-  float *lead = nullptr;
-  unsigned *lead_flag = nullptr;
-  if ((rc = ctx_alloc_t(ctx, &lead, (size_t)grid * 16, "decode split-tile pieces")) ||
-      (rc = ctx_alloc_t(ctx, &lead_flag, (size_t)grid, "decode split-tile flags")))
-    return rc;
+
   CK(cudaMemcpy(d_plan, plan.data(), plan.size() * sizeof(PPhase), cudaMemcpyHostToDevice));
   int *d_cancel = nullptr;
   CK(cudaHostGetDevicePointer((void **)&d_cancel, ctx->h_io + IO_CANCEL, 0));
@@ -687,8 +683,6 @@ static int build_persist_plan(wgd_ctx *ctx) {
   a.xs_bytes = xs;
   a.nsp_max = nsp_max;
   a.l2_ahead = 0;
-  a.lead = lead;
-  a.lead_flag = lead_flag;
   a.tp = tpn;
   a.rank = ctx->tp_rank;
   a.vocab0 = ctx->vocab0;
@@ -701,12 +695,10 @@ static int build_persist_plan(wgd_ctx *ctx) {
 
 // Runs `steps` greedy tokens from (first, start) in one launch; the tokens land in
 // d_tokens and the status words in h_io[IO_STATUS..]. Stream-ordered (no sync).
-// Per-launch state of the persistent kernel: the grid-barrier counter and the split-tile flags
-// start at zero; under tensor parallelism, the peers' exchange buffers and the cross-rank counter
-// base of this launch.
+// Per-launch state of the persistent kernel: the grid-barrier counter starts at zero; under tensor
+// parallelism, the peers' exchange buffers and the cross-rank counter base of this launch.
 static int persist_prepare(wgd_ctx *ctx, PersistArgs &a) {
   CK(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), ctx->stream));  // the arrival counter grows from 0 within a launch
-  CK(cudaMemsetAsync(a.lead_flag, 0, sizeof(unsigned) * ctx->sm_count, ctx->stream));
   if (ctx->tp_size > 1) {
     if (ctx->tp_broken)
       return fail(WGD_ETIMEOUT, "a tensor-parallel peer did not answer within the wait limit earlier; reload the model");

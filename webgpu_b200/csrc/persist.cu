@@ -135,16 +135,14 @@ __device__ __forceinline__ void bar_comp() { asm volatile("bar.sync 3, %0;" ::"n
 __device__ __forceinline__ int chunk_bytes(int type) { return type == Q4_K ? 2304 : 3360; }
 __device__ __forceinline__ int slot_units(int type) { return P_SLOT_BYTES / chunk_bytes(type); }
 
-// CTA c owns units [U*c/grid, U*(c+1)/grid) of the phase's U = tiles * nkb units (tile-major, k
-// blocks in order inside a tile): every CTA gets the same number of units to within one. A tile
-// cut between CTAs is finished by the CTA that holds its first unit, which adds the pieces of the
-// following CTAs in k order (the lead sums), so every output has one fixed summation order.
-__device__ __forceinline__ int unit_at(int tiles, int nkb, int grid, int c) {
-  return (int)((long long)tiles * nkb * c / grid);
-}
+// CTA c owns whole output tiles [tiles*c/grid, tiles*(c+1)/grid): no tile is cut between CTAs, so
+// each output is summed in k order by one CTA with no cross-CTA reduction. (A partition into equal
+// unit counts with the cut tiles finished by their first CTA was measured: the fix-up's L2 round
+// trips at the end of every phase cost more than the balance gained, 733 vs 656 us per token on the
+// 8-layer model.)
 __device__ __forceinline__ void unit_range(int tiles, int nkb, int grid, int c, int &u0, int &u1) {
-  u0 = unit_at(tiles, nkb, grid, c);
-  u1 = unit_at(tiles, nkb, grid, c + 1);
+  u0 = (int)((long long)tiles * c / grid) * nkb;
+  u1 = (int)((long long)tiles * (c + 1) / grid) * nkb;
 }
 
 // better(a, b): a is a finite logit with a higher value, or equal value and lower index
@@ -529,40 +527,6 @@ __device__ __forceinline__ void p_epilogue(GemvCtx &C, int t, float v, int lane)
   }
 }
 
-// ------------------------------------------------------------------ split tiles
-
-__device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// The sum of this CTA's first piece of a tile that started in an earlier CTA's range, for
-// the CTA that finishes the tile (epilogue warp; lane r < 16 holds row r).
-__device__ void p_lead_store(const PersistArgs &a, int c, float v, unsigned tag, int lane) {
-  if (lane < 16) __stcg(a.lead + (size_t)c * 16 + lane, v);
-  __threadfence();
-  __syncwarp();
-  if (lane == 0) st_release_gpu(a.lead_flag + c, tag);
-}
-
-// Waits (bounded) until CTA c2 has published its lead piece of phase `tag`; false when the grid
-// is winding down or the wait ran out (then status[0] = 1 and the stop flag is raised).
-__device__ bool p_lead_wait(const unsigned *lead_flag, int *status, int c2, unsigned tag, volatile int *stop);
-
-// The pieces of tile t_end that the CTAs after c computed (in k order), summed; a real call, so
-// that the epilogue warp's stage loop keeps its registers. A wait that runs out raises *stop.
-__device__ __noinline__ float p_fetch_pieces(const float *lead, const unsigned *lead_flag, int *status, int tiles, int nkb, int c,
-                                             int grid, int t_end, unsigned tag, volatile int *stop, int lane) {
-  float sum = 0.f;
-  for (int c2 = c + 1; c2 < grid; c2++) {
-    const int v0 = unit_at(tiles, nkb, grid, c2);
-    if (v0 >= (t_end + 1) * nkb) break;
-    if (unit_at(tiles, nkb, grid, c2 + 1) == v0) continue;  // an empty range holds no piece
-    if (!p_lead_wait(lead_flag, status, c2, tag, stop)) break;  // the stop flag is raised
-    sum += __ldcg(lead + (size_t)c2 * 16 + (lane & 15));
-  }
-  return sum;
-}
-
 // ------------------------------------------------------------------ attention item
 
 // One (kv head, key split) of decode attention by consumer warps 0..3 (128
@@ -901,21 +865,6 @@ __device__ bool mbar_wait(uint64_t *b, unsigned par, volatile int *stop, int *st
   return true;
 }
 
-__device__ bool p_lead_wait(const unsigned *lead_flag, int *status, int c2, unsigned tag, volatile int *stop) {
-  const uint64_t t0 = gtime();
-  for (unsigned it = 1; (int)(ld_acquire(lead_flag + c2) - tag) < 0; it++) {
-    if ((it & 63) == 0) {
-      if (*stop) return false;
-      if (gtime() - t0 > P_TIMEOUT_NS) {
-        atomicCAS(status, 0, 1);
-        *stop = 1;
-        return false;
-      }
-    }
-  }
-  return true;
-}
-
 // Barrier over every CTA of every rank of a tensor-parallel group, after this CTA's partial rows
 // were pushed to the peers: each CTA adds 1 to the arrival counter in every rank's exchange
 // buffer (system-scope release, after a system-scope fence), then polls its own rank's counter
@@ -1235,31 +1184,10 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
         C.best_v = -FLT_MAX;
         C.best_i = -1;
         C.row0 = a.tp > 1 && pg.argmax ? a.vocab0 : 0;
-        int t = nkb ? u0 / nkb : 0, kbe = nkb ? u0 % nkb : 0;
-        const int lead_t = kbe ? t : -1;  // this range starts inside tile t: its piece goes to the tile's owner
-        const unsigned tag = (unsigned)q + 1u;
-        // the range ends inside a tile that starts in it: this CTA owns that tile, and the pieces of
-        // the following CTAs (computed at the start of their ranges) are fetched before the last
-        // stage's results arrive, so the L2 round trips overlap that stage
-        const int t_end = nkb ? u1 / nkb : 0;
-        const bool tail_owner = nkb && u1 > u0 && u1 % nkb != 0 && t_end * nkb >= u0;
-        float pieces = 0.f;
-        bool fetched = false, ok = true;
+        int t = nkb ? u0 / nkb : 0, kbe = 0;
         float run = 0.f;
-        auto fetch_pieces = [&]() {
-          fetched = true;
-          pieces = p_fetch_pieces(a.lead, a.lead_flag, a.status, pg.tiles, nkb, c, grid, t_end, tag, stop, lane);
-          if (*stop) ok = false;
-        };
-        auto emit = [&](int tt, float vv) {
-          if (tt == lead_t) p_lead_store(a, c, vv, tag, lane);
-          else p_epilogue(C, tt, vv, lane);
-        };
         for (int s0 = u0; s0 < u1; s0 += k, g++) {
           const int n = min(k, u1 - s0), rs = g % P_RES_STAGES;
-          // (not when the last stage is also the first: the following CTA may itself publish its
-          // piece only after its single stage, and a chain of such waits would run serially)
-          if (tail_owner && s0 + k >= u1 && s0 > u0 && ok) fetch_pieces();
           if (mbar_wait(R.done + rs, (g / P_RES_STAGES) & 1u, stop, a.status)) {
             float v[P_STAGE_UNITS];
 #pragma unroll
@@ -1281,8 +1209,8 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
                   if (j == e2) { o2 = run; run = 0.f; }
                 }
               }
-              if (e1 < n) emit(t++, o1);
-              if (e2 < n) emit(t++, o2);
+              if (e1 < n) p_epilogue(C, t++, o1, lane);
+              if (e2 < n) p_epilogue(C, t++, o2, lane);
               kbe += n;
               while (kbe >= nkb) kbe -= nkb;
             } else {
@@ -1292,7 +1220,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
                 if (j < n) {
                   run += v[j];
                   if (++kbe == nkb) {
-                    emit(t++, run);
+                    p_epilogue(C, t++, run, lane);
                     run = 0.f;
                     kbe = 0;
                   }
@@ -1300,19 +1228,8 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
               }
             }
           } else {
-            ok = false;
             __syncwarp();
             if (lane == 0) mbar_arrive(R.resfree + rs);
-          }
-        }
-        // a tile cut at the end of this range: a piece for its owner, or (owner) the tile's end
-        // with the pieces of the following CTAs added
-        if (ok && nkb && kbe != 0 && u1 > u0) {
-          if (t == lead_t) {
-            p_lead_store(a, c, run, tag, lane);
-          } else {
-            if (!fetched) fetch_pieces();
-            if (ok) p_epilogue(C, t, run + pieces, lane);  // own units, then the pieces summed in k order
           }
         }
         if (lane == 0) P_TRACE(step, p, 3);

@@ -77,11 +77,6 @@ struct PersistArgs {
   int *status;          // [0] 0 ok, 1 wait limit hit, 2 non-finite logits, 3 cancelled; [1] steps done
   int nstage, xs_bytes, nsp_max;
   int l2_ahead;  // ring stages requested into L2 ahead of the shared-memory copies (0: none)
-  // split tiles: a CTA's unit range may start inside a tile; the sum of that first piece goes to
-  // lead[c][16] with lead_flag[c] = phase sequence number + 1, and the CTA that holds the start of
-  // the tile adds it (in k order) before the tile's epilogue
-  float *lead;          // [grid][16]
-  unsigned *lead_flag;  // [grid], zero at launch
   // tensor parallelism (tp > 1): every rank's exchange buffer (own included), mapped here
   int tp, rank, vocab0;
   char *xbuf[P_TP_MAX];
