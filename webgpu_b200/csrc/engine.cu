@@ -682,7 +682,11 @@ static int build_persist_plan(wgd_ctx *ctx) {
   a.nstage = ns;
   a.xs_bytes = xs;
   a.nsp_max = nsp_max;
-  a.l2_ahead = 0;
+  // four ring stages of the weight stream are also requested into L2 ahead of their shared-memory
+  // copies (measured on the 8-layer model, 0 / 4 / 8 / 16 / 24 stages: 735 / 723 / 727 / 805 / 800 us
+  // per token in one build, 660 / 653 for 0 / 4 in another; deeper look-ahead competes with the loads
+  // of the latency-bound phases)
+  a.l2_ahead = 4;
   a.tp = tpn;
   a.rank = ctx->tp_rank;
   a.vocab0 = ctx->vocab0;

@@ -490,7 +490,11 @@ struct GemvCtx {
   float best_v;  // greedy tracking (per lane)
   int best_i;
   int row0;      // global index of output row 0 (the vocabulary offset of this rank's LM head rows)
+  // residual-add epilogues: this lane's rows of the CTA's first P_PRE tiles, loaded at phase start
+  int pre_t0;
+  float pre[4];
 };
+constexpr int P_PRE = 4;
 
 // Epilogue of one finished tile: lane r < 16 holds the value of tile row r.
 __device__ __forceinline__ void p_epilogue(GemvCtx &C, int t, float v, int lane) {
@@ -512,7 +516,9 @@ __device__ __forceinline__ void p_epilogue(GemvCtx &C, int t, float v, int lane)
       return;
     }
     if (g.epi == EPI_ADD) {
-      val = __ldcg(g.y + row) + val;
+      const int k = t - C.pre_t0;
+      const float old = k == 0 ? C.pre[0] : k == 1 ? C.pre[1] : k == 2 ? C.pre[2] : k == 3 ? C.pre[3] : __ldcg(g.y + row);
+      val = old + val;
       g.y[row] = val;
     } else if (g.epi == EPI_SILU) {
       val = g2_silu(val);
@@ -1185,6 +1191,14 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
         C.best_i = -1;
         C.row0 = a.tp > 1 && pg.argmax ? a.vocab0 : 0;
         int t = nkb ? u0 / nkb : 0, kbe = 0;
+        // the residual rows this CTA will add into are final before the phase starts (only this CTA
+        // writes them in it): load them now, off the phase's tail
+        C.pre_t0 = t;
+#pragma unroll
+        for (int k2 = 0; k2 < P_PRE; k2++) {
+          const int row = (t + k2) * 16 + lane;
+          C.pre[k2] = pg.epi == EPI_ADD && lane < 16 && (t + k2) * nkb < u1 && row < pg.rows ? __ldcg(pg.y + row) : 0.f;
+        }
         float run = 0.f;
         for (int s0 = u0; s0 < u1; s0 += k, g++) {
           const int n = min(k, u1 - s0), rs = g % P_RES_STAGES;
