@@ -904,8 +904,111 @@ def case_c2() -> None:
     print(json.dumps(c2_table(0)), flush=True)
 
 
+def case_gemma_tp(steps: int = 16) -> None:
+    """The benchmark's Gemma-3-27B configuration resident and tensor-parallel over the ranks of a
+    torchrun launch (one rank: one GPU): 62 gemma3 blocks (5 local : 1 global, Q/K norm, GeGLU),
+    seed 3, the 1024-token prompt prefilled in batches of 128, then `steps` greedy tokens of the
+    device decode loop (CUDA events, max over ranks). Parity: a 4-token prompt at position 0 and 3
+    greedy tokens, the full logits gathered to rank 0 and compared with the float64 oracle there.
+    Rank 0 prints one JSON object."""
+    import datetime
+
+    import torch
+    from webgpu_b200 import _native, synth
+    from webgpu_b200.engine import PagedEngine
+    from webgpu_b200.source import MemorySource
+    world, rank, local = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist, host_group = None, None
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=torch.device("cuda", local))
+        host_group = tdist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=900))
+        dist = tdist
+
+    def host_barrier():
+        if dist:
+            dist.barrier(group=host_group)
+    try:
+        t0 = time.time()
+        spec = synth.baseline_spec(4)
+        path = None
+        if world > 1:
+            base = "/dev/shm" if os.path.isdir("/dev/shm") and shutil.disk_usage("/dev/shm").free > 40e9 else tempfile.gettempdir()
+            path = os.path.join(base, f"wgd_bench_gemma3_27b_seed3_{os.environ.get('MASTER_PORT', '0')}.gguf")
+        image = None
+        if local == 0:
+            image = synth.build_gguf(spec)
+            if path:
+                image.tofile(path + ".tmp")
+                os.replace(path + ".tmp", path)
+        host_barrier()
+        if image is None:
+            image = np.memmap(path, dtype=np.uint8, mode="r")
+        log(f"[gemma_tp] rank {rank}: model ready in {time.time() - t0:.1f}s ({image.nbytes / 1e9:.2f} GB)")
+        opts = {"contextLength": 2048, "batchSize": 128, "performance": "fast", "gpuBudgetMiB": 60 * 1024,
+                "tensorParallel": world, "rank": rank, "device": local}
+        if dist:
+            def exchange(b: bytes):
+                out = [None] * world
+                dist.all_gather_object(out, b, group=host_group)
+                return out
+            opts["exchange"] = exchange
+        eng = PagedEngine()
+        eng.load(MemorySource(image), opts)
+        host_barrier()
+        if path and local == 0:
+            os.unlink(path)
+        L = _native.lib()
+        prompt = spec.prompt[:1024]
+        st = _native.StatsC()
+        pf_ms, tok = 0.0, None
+        for i in range(0, len(prompt), 128):
+            tok = eng.forward(prompt[i:i + 128], i, i + 128 == len(prompt))
+            L.wgd_stats_get(eng.ctx, ctypes.byref(st))
+            pf_ms += st.last_forward_ms
+        buf = (ctypes.c_int32 * max(steps, 3))()
+        _native.check(L.wgd_decode(eng.ctx, tok, len(prompt), 3, buf), "decode")  # warm-up (graph capture)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        _native.check(L.wgd_decode(eng.ctx, tok, len(prompt), steps, buf), "decode")
+        L.wgd_stats_get(eng.ctx, ctypes.byref(st))
+        ms = st.last_forward_ms
+        if dist:
+            t = torch.tensor([ms, pf_ms], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms, pf_ms = float(t[0]), float(t[1])
+        why = ctypes.create_string_buffer(256)
+        persistent = L.wgd_persistent_status(eng.ctx, why, 256) == 1
+        gpu = parity_gpu(eng, list(spec.prompt[:PARITY_PROMPT]), 3)
+        par = None
+        if rank == 0:
+            rt, rl, _, _, _ = parity_oracle(image, list(spec.prompt[:PARITY_PROMPT]), 3, cpu_threads(), False)
+            par = parity_summary(gpu, rt, rl)
+        host_barrier()
+        c = eng.config
+        wbytes = weight_bytes(eng.gguf, c)
+        eng.dispose()
+        if rank == 0:
+            peak, kind = peaks()
+            step_ms = ms / steps
+            achieved = wbytes / world / (step_ms / 1000) / 1e9
+            print(json.dumps({"workload": "Gemma-3-27B arch Q4_K_M, 1024-token prompt in batches of 128, then batch-1 greedy decode",
+                              "n_gpus": world, "steps": steps, "tok_per_s": steps / (ms / 1000.0), "ms_per_step": step_ms,
+                              "prefill_ms": pf_ms, "prefill_tok_per_s": len(prompt) / (pf_ms / 1000.0),
+                              "weight_bytes_per_rank": wbytes / world, "achieved_gbs_per_rank": achieved,
+                              "frac": achieved / peak, "peak_kind": kind,
+                              "path": "persistent kernel" if persistent else f"per-kernel CUDA graph ({why.value.decode()})",
+                              "parity": par}), flush=True)
+    finally:
+        if dist:
+            dist.destroy_process_group()
+
+
 CASES = {"gemv": case_gemv, "attention": case_attention, "decode": case_decode, "gemm": case_gemm,
-         "prefill": case_prefill, "qwen": case_qwen, "gemma_paged": case_gemma_paged, "c2": case_c2}
+         "prefill": case_prefill, "qwen": case_qwen, "gemma_paged": case_gemma_paged, "c2": case_c2,
+         "gemma_tp": case_gemma_tp}
 
 
 # ------------------------------------------------------------------ main

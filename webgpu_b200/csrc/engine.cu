@@ -552,7 +552,8 @@ static int build_persist_plan(wgd_ctx *ctx) {
   // tensor parallelism: the summed input row of a phase (hidden plus the peers' partials) sits in
   // shared memory behind that phase's digit records
   const int row_cols = tpn > 1 ? H : 0;
-  const int ns = persist_max_stages(max_cols, G, hd, row_cols);
+  int ns = persist_max_stages(max_cols, G, hd, row_cols);
+  if (const char *v = getenv("WGD_PERSIST_STAGES")) ns = std::min(ns, std::max(3, atoi(v)));  // tuning override
   if (ns < 3) return no("not enough shared memory for the weight ring");
   int xs = 0;
   const size_t smem = persist_smem_bytes(max_cols, G, hd, ns, &xs, row_cols);

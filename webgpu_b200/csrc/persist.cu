@@ -201,38 +201,56 @@ __device__ __forceinline__ PLane p_lane(int lane) {
   return L;
 }
 
-// Digitise the phase input (RMS-normalised when nw is set) with one round of L2
-// loads: warp w holds super-blocks w, w+16, ... in registers, the norm's sum of
-// squares comes from the same registers. x ~= s * (a + b/254 + c/254^2), s =
-// max|x|/127 per super-block (the same digits as the stand-alone GEMV).
+// Digitise the phase input (RMS-normalised when nw is set) with one round of loads: warp w
+// holds super-blocks w, w+14, ... in registers, lane l the eight values 8(l&3)..8(l&3)+7 of
+// 32-block l>>2, and the norm's sum of squares comes from the same registers. x ~= s * (a + b/254 +
+// c/254^2), s = max|x|/127 per super-block (the same digits as the stand-alone GEMV). The block
+// maximum is one warp reduction over the bit patterns (non-negative floats order as integers), the
+// digit bytes are packed from the bit patterns of the rounding additions, and a 32-block's digit
+// sums meet over the four lanes that hold it (a 16-run's over two).
 // SM: x is a row in this CTA's shared memory (the tensor-parallel sum, p_sum_parts), else in global
 // memory (read through L2).
+__device__ __forceinline__ void digits254_bits(float t, uint32_t &a, uint32_t &b, uint32_t &c) {
+  // digits254 without the final masks: each digit is the low byte of the returned bit pattern
+  const float M = 12582912.f;
+  const float ta = __fadd_rn(t, M), r1 = __fmul_rn(__fsub_rn(t, __fsub_rn(ta, M)), 254.f);
+  const float tb = __fadd_rn(r1, M), r2 = __fmul_rn(__fsub_rn(r1, __fsub_rn(tb, M)), 254.f);
+  const float tc = __fadd_rn(r2, M);
+  a = __float_as_uint(ta);
+  b = __float_as_uint(tb);
+  c = __float_as_uint(tc);
+}
+// the low bytes of w0..w3 as one word (byte e from w_e)
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+  return __byte_perm(__byte_perm(w0, w1, 0x0040), __byte_perm(w2, w3, 0x0040), 0x5410);
+}
+
 template <bool SM>
 __device__ void p_digitise(const float *x, const float *nw, float eps, int cols, bool q6, const PX &X, float *red, int *sums,
                            int warp, int lane) {
   const int nsb = cols >> 8;
-  const int q8 = lane & 7, tg = q8 & 3, hi = q8 >> 2;
+  const int j = lane >> 2, q = lane & 3;  // 32-block, quarter (eight values k = 8q..8q+7)
   float4 v[P_MAXSBW][2];
 #pragma unroll
   for (int i = 0; i < P_MAXSBW; i++) {
     const int sb = warp + P_CWARPS * i;
+    const int col = 256 * sb + 32 * j + 8 * q;
+    const bool in = sb < nsb;
 #pragma unroll
-    for (int p = 0; p < 2; p++) {
-      const int col = 256 * sb + 32 * ((lane >> 3) + 4 * p) + 4 * q8;
-      const bool in = sb < nsb;
-      if (SM) v[i][p] = in ? *reinterpret_cast<const float4 *>(x + col) : make_float4(0.f, 0.f, 0.f, 0.f);
-      else v[i][p] = in ? __ldcg(reinterpret_cast<const float4 *>(x + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
-      // the norm weights are read after the block-wide sum: bring them into L1 now
-      if (in && nw) asm volatile("prefetch.global.L1 [%0];" ::"l"(nw + col));
+    for (int h = 0; h < 2; h++) {
+      if (SM) v[i][h] = in ? *reinterpret_cast<const float4 *>(x + col + 4 * h) : make_float4(0.f, 0.f, 0.f, 0.f);
+      else v[i][h] = in ? __ldcg(reinterpret_cast<const float4 *>(x + col + 4 * h)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    // the norm weights are read after the block-wide sum: bring them into L1 now
+    if (in && nw) asm volatile("prefetch.global.L1 [%0];" ::"l"(nw + col));
   }
   if (nw) {
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < P_MAXSBW; i++)
 #pragma unroll
-      for (int p = 0; p < 2; p++)
-        ss = fmaf(v[i][p].x, v[i][p].x, fmaf(v[i][p].y, v[i][p].y, fmaf(v[i][p].z, v[i][p].z, fmaf(v[i][p].w, v[i][p].w, ss))));
+      for (int h = 0; h < 2; h++)
+        ss = fmaf(v[i][h].x, v[i][h].x, fmaf(v[i][h].y, v[i][h].y, fmaf(v[i][h].z, v[i][h].z, fmaf(v[i][h].w, v[i][h].w, ss))));
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
     bar_comp();
@@ -244,52 +262,52 @@ __device__ void p_digitise(const float *x, const float *nw, float eps, int cols,
     for (int i = 0; i < P_MAXSBW; i++) {
       const int sb = warp + P_CWARPS * i;
       if (sb >= nsb) continue;
+      const int col = 256 * sb + 32 * j + 8 * q;
 #pragma unroll
-      for (int p = 0; p < 2; p++) {
-        const int col = 256 * sb + 32 * ((lane >> 3) + 4 * p) + 4 * q8;
-        const float4 w = __ldg(reinterpret_cast<const float4 *>(nw + col));
-        v[i][p] = make_float4(v[i][p].x * inv * w.x, v[i][p].y * inv * w.y, v[i][p].z * inv * w.z, v[i][p].w * inv * w.w);
+      for (int h = 0; h < 2; h++) {
+        const float4 w = __ldg(reinterpret_cast<const float4 *>(nw + col + 4 * h));
+        v[i][h] = make_float4(v[i][h].x * inv * w.x, v[i][h].y * inv * w.y, v[i][h].z * inv * w.z, v[i][h].w * inv * w.w);
       }
     }
   }
+  // record words of this lane: plane dg, k = 8q..8q+3 at tig 2(q&1), k = 8q+4.. at tig 2(q&1)+1,
+  // half hi = q >> 1 (k >= 16), 32-block j
+  const int tg0 = 2 * (q & 1), hi = q >> 1;
 #pragma unroll
   for (int i = 0; i < P_MAXSBW; i++) {
     const int sb = warp + P_CWARPS * i;
     if (sb >= nsb) continue;
-    float amax = 0.f;
-#pragma unroll
-    for (int p = 0; p < 2; p++)
-      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i][p].x), fabsf(v[i][p].y)), fmaxf(fabsf(v[i][p].z), fabsf(v[i][p].w))));
-    amax = warp_max(amax);
+    float m = fmaxf(fmaxf(fmaxf(fabsf(v[i][0].x), fabsf(v[i][0].y)), fmaxf(fabsf(v[i][0].z), fabsf(v[i][0].w))),
+                    fmaxf(fmaxf(fabsf(v[i][1].x), fabsf(v[i][1].y)), fmaxf(fabsf(v[i][1].z), fabsf(v[i][1].w))));
+    const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
     // digit scale: the fast reciprocal is within 2 ulp of 127 / amax, which only moves the
     // digits by that much relative to the exact scale sxs they are multiplied back with
     const float sc = amax > 0.f ? __fdividef(127.f, amax) : 0.f;
     if (lane == 0) X.sxs[sb] = amax > 0.f ? amax / 127.f : 0.f;
+    uint32_t wa[3][2];  // [plane][word]
 #pragma unroll
-    for (int p = 0; p < 2; p++) {
-      const int j = (lane >> 3) + 4 * p;
-      const float xs4[4] = {v[i][p].x, v[i][p].y, v[i][p].z, v[i][p].w};
-      uint32_t pk[3] = {0u, 0u, 0u};
+    for (int h = 0; h < 2; h++) {
+      uint32_t a0, b0, c0, a1, b1, c1, a2, b2, c2, a3, b3, c3;
+      digits254_bits(v[i][h].x * sc, a0, b0, c0);
+      digits254_bits(v[i][h].y * sc, a1, b1, c1);
+      digits254_bits(v[i][h].z * sc, a2, b2, c2);
+      digits254_bits(v[i][h].w * sc, a3, b3, c3);
+      wa[0][h] = pack_low_bytes(a0, a1, a2, a3);
+      wa[1][h] = pack_low_bytes(b0, b1, b2, b3);
+      wa[2][h] = pack_low_bytes(c0, c1, c2, c3);
+    }
+    uint8_t *rec = X.brec + (size_t)sb * 960 + j * 8 + hi * 4;
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        uint32_t da, db, dc;
-        digits254(xs4[e] * sc, da, db, dc);
-        pk[0] |= da << (8 * e);
-        pk[1] |= db << (8 * e);
-        pk[2] |= dc << (8 * e);
-      }
-#pragma unroll
-      for (int dg = 0; dg < 3; dg++) {
-        *reinterpret_cast<uint32_t *>(X.brec + (size_t)sb * 960 + (dg * 4 + tg) * 80 + j * 8 + hi * 4) = pk[dg];
-        int s16 = __dp4a((int)pk[dg], 0x01010101, 0);  // this quad's digit sum
-        s16 += __shfl_xor_sync(0xffffffffu, s16, 1);
-        s16 += __shfl_xor_sync(0xffffffffu, s16, 2);   // 16-run 2j + hi
-        const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 4);  // 32-block j
-        if (q6) {
-          if ((q8 & 3) == 0) sums[dg * 16 + 2 * j + hi] = s16;
-        } else if (q8 == 0) {
-          sums[dg * 16 + j] = s32;
-        }
+    for (int dg = 0; dg < 3; dg++) {
+      *reinterpret_cast<uint32_t *>(rec + (dg * 4 + tg0) * 80) = wa[dg][0];
+      *reinterpret_cast<uint32_t *>(rec + (dg * 4 + tg0 + 1) * 80) = wa[dg][1];
+      int s = __dp4a((int)wa[dg][0], 0x01010101, __dp4a((int)wa[dg][1], 0x01010101, 0));
+      s += __shfl_xor_sync(0xffffffffu, s, 1);  // 16-run 2j + hi
+      if (q6) {
+        if ((q & 1) == 0) sums[dg * 16 + 2 * j + hi] = s;
+      } else {
+        s += __shfl_xor_sync(0xffffffffu, s, 2);  // 32-block j
+        if (q == 0) sums[dg * 16 + j] = s;
       }
     }
     __syncwarp();
@@ -300,10 +318,10 @@ __device__ void p_digitise(const float *x, const float *nw, float eps, int cols,
       uint32_t lo = 0u, hw = 0u;
       if (grp < 3 && (q6 || tig < 2)) {
 #pragma unroll
-        for (int m = 0; m < 4; m++) {
-          const int sv = sums[grp * 16 + 4 * tig + m];
-          lo |= ((uint32_t)sv & 255u) << (8 * m);
-          hw |= ((uint32_t)(sv >> 8) & 255u) << (8 * m);
+        for (int m2 = 0; m2 < 4; m2++) {
+          const int sv = sums[grp * 16 + 4 * tig + m2];
+          lo |= ((uint32_t)sv & 255u) << (8 * m2);
+          hw |= ((uint32_t)(sv >> 8) & 255u) << (8 * m2);
         }
       }
       *reinterpret_cast<uint2 *>(X.dsw + (size_t)sb * 256 + lane * 8) = make_uint2(lo, hw);
