@@ -867,8 +867,7 @@ struct Ring {
 
 // Waits for phase `par` of mbarrier b. False when the grid is winding down or this
 // wait ran out (then status[0] = 1 and the stop flag is raised).
-__device__ bool mbar_wait(uint64_t *b, unsigned par, volatile int *stop, int *status) {
-  if (mbar_test(b, par)) return true;
+__device__ __noinline__ bool mbar_wait_slow(uint64_t *b, unsigned par, volatile int *stop, int *status) {
   const uint64_t t0 = gtime();
 #ifdef WGD_PERSIST_TRACE
   struct Acc {
@@ -887,6 +886,9 @@ __device__ bool mbar_wait(uint64_t *b, unsigned par, volatile int *stop, int *st
     }
   }
   return true;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, unsigned par, volatile int *stop, int *status) {
+  return mbar_test(b, par) || mbar_wait_slow(b, par, stop, status);
 }
 
 // Barrier over every CTA of every rank of a tensor-parallel group, after this CTA's partial rows
@@ -1003,21 +1005,35 @@ __device__ void producer(const PersistArgs &a, const Ring &R, volatile int *stop
   SIt pf = f;
   bool fv = sit_seek(a, grid, c, f), pv = sit_seek(a, grid, c, pf);
   int ahead = 0;
-  unsigned g = 0;
+  unsigned g = 0, epar = 1u;  // stages issued; the parity that frees the current slot
+  int slot = 0;
   while (fv) {
     while (pv && ahead < a.l2_ahead) {
       prefetch_l2(pf.w + (size_t)pf.s0 * pf.CB, (unsigned)(min(pf.k, pf.u1 - pf.s0) * pf.CB));
       pv = sit_next(a, grid, c, pf);
       ahead++;
     }
-    const int slot = g % R.ns;
-    if (!mbar_wait(R.empty + slot, ((g / R.ns) & 1u) ^ 1u, stop, a.status)) break;
+#ifdef WGD_PERSIST_TRACE
+    const uint64_t tw0 = gtime();
+#endif
+    if (!mbar_wait(R.empty + slot, epar, stop, a.status)) break;
+#ifdef WGD_PERSIST_TRACE
+    // time this producer waited for a free slot, per phase (slot 7)
+    if ((blockIdx.x == 0 || blockIdx.x == 100) && f.step < TR_STEPS && f.p < TR_PHASES) {
+      uint64_t &w = g_trace[blockIdx.x == 0 ? 0 : 1][f.step][f.p][7];
+      w = (f.s0 == f.u0 ? 0 : w) + (gtime() - tw0);
+    }
+#endif
     const int n = min(f.k, f.u1 - f.s0);
     if (f.s0 == f.u0) P_TRACE(f.step, f.p, 4);
     if (f.s0 + f.k >= f.u1) P_TRACE(f.step, f.p, 5);
     mbar_expect_tx(R.full + slot, (unsigned)(n * f.CB));
     bulk_g2s(R.slots + (size_t)slot * P_SLOT_BYTES, f.w + (size_t)f.s0 * f.CB, (unsigned)(n * f.CB), R.full + slot);
     g++;
+    if (++slot == R.ns) {
+      slot = 0;
+      epar ^= 1u;
+    }
     fv = sit_next(a, grid, c, f);
     ahead--;
   }
@@ -1157,41 +1173,44 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
         const PLane PL = p_lane(lane);
         // this warp's chunks: u0 + warp, u0 + warp + P_CWARPS, ... (tile t, super-block kb)
         int nu = u0 + warp, kb = nkb ? nu % nkb : 0;
+        // ring slot and its fill parity, advanced with g (no division per stage)
+        int slot = (int)(g % (unsigned)R.ns);
+        unsigned fpar = (g / (unsigned)R.ns) & 1u;
         for (int s0 = u0; s0 < u1; s0 += k, g++) {
-          const int s1 = min(u1, s0 + k), slot = g % R.ns, rs = g % P_RES_STAGES;
-          // this warp's chunks of the stage (at most one: k <= P_CWARPS), result kept in registers
-          float r[1][2] = {{0.f, 0.f}};
-          int nmine = 0;
-          const int first = nu;
-          if (mbar_wait(R.full + slot, (g / R.ns) & 1u, stop, a.status)) {
-            const uint8_t *base = R.slots + (size_t)slot * P_SLOT_BYTES;
-            for (; nu < s1; nu += P_CWARPS, nmine++) {
+          const int s1 = min(u1, s0 + k), rs = g % P_RES_STAGES;
+          // this warp's chunk of the stage (at most one: k <= P_CWARPS). After the reduction over the
+          // four lanes of an MMA row group, lane 4i holds row i and lane 4i+1 row i+8.
+          float v = 0.f;
+          const bool mine = nu < s1;
+          const int at = nu - s0;
+          const bool ok = mbar_wait(R.full + slot, fpar, stop, a.status);
+          if (ok) {
+            if (mine) {
               float acc[2] = {0.f, 0.f};
-              const uint8_t *cp = base + (size_t)(nu - s0) * CB;
+              const uint8_t *cp = R.slots + (size_t)slot * P_SLOT_BYTES + (size_t)at * CB;
               if (q6) p_q6k(cp, kb, X, PL, lane, acc);
               else p_q4k(cp, kb, X, PL, lane, acc);
-              acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 1);
-              acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 2);
-              acc[1] += __shfl_xor_sync(0xffffffffu, acc[1], 1);
-              acc[1] += __shfl_xor_sync(0xffffffffu, acc[1], 2);
-              r[0][0] = acc[0];
-              r[0][1] = acc[1];
+              // (a0 + a1) + (a2 + a3) for each row, as two shuffles: even lanes keep row i, odd
+              // lanes row i+8, and each sends the other row's partial to its neighbour
+              const bool odd = lane & 1;
+              v = odd ? acc[1] : acc[0];
+              v += __shfl_xor_sync(0xffffffffu, odd ? acc[0] : acc[1], 1);
+              v += __shfl_xor_sync(0xffffffffu, v, 2);
               kb += P_CWARPS;
               while (kb >= nkb) kb -= nkb;
             }
-          } else {
-            while (nu < s1) nu += P_CWARPS;  // winding down: keep the unit cursor in step
           }
+          if (mine) nu += P_CWARPS;
           __syncwarp();
           if (lane == 0) mbar_arrive(R.empty + slot);  // the weight slot may be refilled
-          if (mbar_wait(R.resfree + rs, ((g / P_RES_STAGES) & 1u) ^ 1u, stop, a.status) && (lane & 3) == 0) {
-            for (int i = 0; i < nmine; i++) {
-              sh.res[rs][first + i * P_CWARPS - s0][lane >> 2] = r[i][0];
-              sh.res[rs][first + i * P_CWARPS - s0][(lane >> 2) + 8] = r[i][1];
-            }
-          }
+          if (mbar_wait(R.resfree + rs, ((g / P_RES_STAGES) & 1u) ^ 1u, stop, a.status) && ok && mine && (lane & 3) < 2)
+            sh.res[rs][at][(lane >> 2) + 8 * (lane & 1)] = v;
           __syncwarp();
           if (lane == 0) mbar_arrive(R.done + rs);
+          if (++slot == R.ns) {
+            slot = 0;
+            fpar ^= 1u;
+          }
         }
         if (tid == 0) P_TRACE(step, p, 2);
 #ifdef WGD_PERSIST_TRACE
