@@ -537,6 +537,7 @@ static int build_persist_plan(wgd_ctx *ctx) {
   if (ctx->tp_size > 1 && ctx->sm_count + 1 > P_CAND_STRIDE) return no("more CTAs than the cross-rank candidate table holds");
   if (c.family == 1) return no("the gemma block (post-norms) uses the per-kernel path");
   const int G = ctx->kv_l ? ctx->heads_l / ctx->kv_l : 0;
+  if (ctx->kv_l > ctx->sm_count) return no("more kv heads than CTAs (one attention item per CTA)");
   if (hd % 16 || hd > 128 || G < 1 || G > 8)
     return no("attention shape outside the persistent kernel (head_dim 16..128 in steps of 16, GQA group <= 8)");
   auto tiled_ok = [](const DevLinear &L) { return L.tiled && L.cols % 256 == 0 && L.cols >= 256; };

@@ -12,11 +12,15 @@
 //    launch, one CTA per SM) with one arrival counter that only grows;
 //  * inside a CTA, the producer warp and the consumer warps share a ring of
 //    shared-memory slots guarded by mbarriers ("full": transaction bytes of the
-//    bulk copy; "empty": one arrival per consumer warp);
+//    bulk copy; "empty": the epilogue warp's arrival once every compute warp has
+//    reported the stage done);
 //  * each CTA owns whole 16-row output tiles; the compute warps hand each
 //    chunk's 16 row sums to the epilogue warp through a ring of result stages
-//    (mbarriers "done" / "resfree"), and the epilogue warp adds a tile's chunks
-//    in k-block order, so every sum has a fixed order.
+//    (mbarrier "done", one arrival per compute warp), and the epilogue warp adds
+//    a tile's chunks in k-block order, so every sum has a fixed order. A result
+//    stage is free again without a barrier of its own: stage g + ns of the
+//    weight ring is only issued after the epilogue warp has read the results of
+//    stage g, and ns <= P_RES_STAGES.
 // Every wait is bounded by a globaltimer deadline; a wait that runs out sets
 // status[0] = 1 and the whole grid winds down (the producer first waits for its
 // copies in flight).
@@ -117,6 +121,7 @@ __device__ uint64_t g_wait_acc[2];  // ns thread 0 of CTAs 0 / 100 spent waiting
 // (sums each tile's chunk results in k-block order, stores, greedy tracking), 15 producer.
 constexpr int P_EWARP = P_CWARPS, P_PWARP = P_CWARPS + 1;
 constexpr int P_MAXSTAGES = 8, P_STAGE_UNITS = 16, P_RES_STAGES = 8;
+static_assert(P_MAXSTAGES <= P_RES_STAGES, "a result stage is recycled through the weight ring (ns <= P_RES_STAGES)");
 static_assert(P_SLOT_BYTES / 2304 <= P_CWARPS && P_SLOT_BYTES / 2304 <= P_STAGE_UNITS, "a stage holds at most one chunk per compute warp");
 
 // Shared state of one CTA besides the ring and the xs region.
@@ -339,10 +344,14 @@ __device__ void p_sum_parts(const float *x, const float *part, int nparts, int s
   for (int c4 = tid; c4 < (cols >> 2); c4 += P_CWARPS * 32) {
     const int col = 4 * c4;
     float4 v = __ldcg(reinterpret_cast<const float4 *>(x + col));
-    for (int j = 0; j < nparts; j++) {
-      const float4 w = __ldcg(reinterpret_cast<const float4 *>(part + (size_t)j * stride + col));
-      v = make_float4(v.x + w.x, v.y + w.y, v.z + w.z, v.w + w.w);
-    }
+    // the partial rows requested together (at most P_TP_MAX), then added in rank order
+    float4 w[P_TP_MAX];
+#pragma unroll
+    for (int j = 0; j < P_TP_MAX; j++)
+      w[j] = j < nparts ? __ldcg(reinterpret_cast<const float4 *>(part + (size_t)j * stride + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < P_TP_MAX; j++)
+      if (j < nparts) v = make_float4(v.x + w[j].x, v.y + w[j].y, v.z + w[j].z, v.w + w[j].w);
     *reinterpret_cast<float4 *>(dst + col) = v;
     if (x_out && (col >> 8) % (int)gridDim.x == (int)blockIdx.x) __stcg(reinterpret_cast<float4 *>(x_out + col), v);
   }
@@ -859,8 +868,8 @@ __device__ float p_embed_value(const PersistArgs &a, int token, int col) {
 // ------------------------------------------------------------------ kernel
 
 struct Ring {
-  uint64_t *full, *empty;    // weight slots: bytes landed / compute warps done with them
-  uint64_t *done, *resfree;  // chunk results (P_RES_STAGES): written by the compute warps / read by the epilogue warp
+  uint64_t *full, *empty;  // weight slots: bytes landed / the stage's results read (epilogue warp)
+  uint64_t *done;          // chunk results (P_RES_STAGES): written by every compute warp
   uint8_t *slots;
   int ns;
 };
@@ -1063,7 +1072,6 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
   R.full = reinterpret_cast<uint64_t *>(smem);
   R.empty = R.full + P_MAXSTAGES;
   R.done = R.empty + P_MAXSTAGES;
-  R.resfree = R.done + P_RES_STAGES;
   R.slots = smem + 256;
   uint8_t *xs = R.slots + (size_t)R.ns * P_SLOT_BYTES;
   PShared &sh = *reinterpret_cast<PShared *>(xs + a.xs_bytes);
@@ -1071,11 +1079,10 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
   if (tid == 0) {
     for (int i = 0; i < R.ns; i++) {
       mbar_init(R.full + i, 1);
-      mbar_init(R.empty + i, P_CWARPS);
+      mbar_init(R.empty + i, 1);
     }
     for (int i = 0; i < P_RES_STAGES; i++) {
       mbar_init(R.done + i, P_CWARPS);
-      mbar_init(R.resfree + i, 1);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1156,9 +1163,9 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
         // the digitisation so that its loads of the phase input do not queue behind these copies
         if (p + 1 < a.nphases && sh.dsc[(q + 1) % 3].kind == PH_ATTN && warp < 4) {
           const PAttn &A = sh.dsc[(q + 1) % 3].a;
-          // (only where the digit records, and a tensor-parallel input row behind them, end below stage 0)
-          const size_t used = pg.xsum ? ((px_bytes(pg.cols) + 15) & ~(size_t)15) + 4 * (size_t)pg.cols : px_bytes(pg.cols);
-          if (used <= (size_t)attn_stage_floats(A.hd) * 4) {
+          // (only where the digit records end below stage 0; a tensor-parallel input row behind them
+          // is no longer read once the records are written)
+          if (px_bytes(pg.cols) <= (size_t)attn_stage_floats(A.hd) * 4) {
             int chunk, nsp;
             attn_split(A, pos, a.nsp_max, chunk, nsp);
             if (c < A.kv_heads * nsp) {
@@ -1201,10 +1208,9 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
             }
           }
           if (mine) nu += P_CWARPS;
-          __syncwarp();
-          if (lane == 0) mbar_arrive(R.empty + slot);  // the weight slot may be refilled
-          if (mbar_wait(R.resfree + rs, ((g / P_RES_STAGES) & 1u) ^ 1u, stop, a.status) && ok && mine && (lane & 3) < 2)
-            sh.res[rs][at][(lane >> 2) + 8 * (lane & 1)] = v;
+          // (result stage rs is free: this stage's weights were issued after the epilogue warp read
+          // stage g - ns, and ns <= P_RES_STAGES)
+          if (ok && mine && (lane & 3) < 2) sh.res[rs][at][(lane >> 2) + 8 * (lane & 1)] = v;
           __syncwarp();
           if (lane == 0) mbar_arrive(R.done + rs);
           if (++slot == R.ns) {
@@ -1237,14 +1243,18 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
           C.pre[k2] = pg.epi == EPI_ADD && lane < 16 && (t + k2) * nkb < u1 && row < pg.rows ? __ldcg(pg.y + row) : 0.f;
         }
         float run = 0.f;
+        int eslot = (int)(g % (unsigned)R.ns);  // the weight slot of stage g
         for (int s0 = u0; s0 < u1; s0 += k, g++) {
-          const int n = min(k, u1 - s0), rs = g % P_RES_STAGES;
+          const int n = min(k, u1 - s0), rs = g % P_RES_STAGES, ws = eslot;
+          if (++eslot == R.ns) eslot = 0;
           if (mbar_wait(R.done + rs, (g / P_RES_STAGES) & 1u, stop, a.status)) {
             float v[P_STAGE_UNITS];
 #pragma unroll
             for (int j = 0; j < P_STAGE_UNITS; j++) v[j] = (j < n && lane < 16) ? sh.res[rs][j][lane] : 0.f;
             __syncwarp();
-            if (lane == 0) mbar_arrive(R.resfree + rs);  // results copied out
+            // every compute warp is done with the weight slot and the results are read: the
+            // producer may refill the slot (and the result stage is free once it has)
+            if (lane == 0) mbar_arrive(R.empty + ws);
             if (nkb >= 8) {
               // the stage's results in k-block order; a tile ends where the running k-block count
               // reaches nkb. With n <= 16 results and nkb >= 8 a stage holds at most two tile ends,
@@ -1280,7 +1290,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
             }
           } else {
             __syncwarp();
-            if (lane == 0) mbar_arrive(R.resfree + rs);
+            if (lane == 0) mbar_arrive(R.empty + ws);
           }
         }
         if (lane == 0) P_TRACE(step, p, 3);
