@@ -5,7 +5,8 @@ The kernel covers dense llama/qwen2/qwen3 blocks whose projections are in the ti
 (Q4_K/Q6_K, input widths >= 2048). These mid-size models are the smallest that qualify; each
 variant exercises one branch of the kernel: GQA groups of 4 and 8, head_dim 64 and 128,
 Q/K norm, Q/K/V and output biases, a tied (embedding) LM head with a ragged last tile, an
-ungated MLP, a sliding window whose ring wraps, and attention split over many CTAs.
+ungated MLP, a sliding window whose ring wraps, attention split over many CTAs, and a head_dim that
+is not a multiple of 32 (the attention item's four-warp form; eight warps otherwise).
 """
 import ctypes
 
@@ -40,6 +41,8 @@ MODELS = {
                                                    extra=[("llama.attention.sliding_window", synth.T_U32, 40)]),
     "qwen2_g8_bias_tied_ragged_head": lambda: _mid("qwen2", seed=25, kv_heads=2, ffn=4864, vocab=3000, bias=True, tied=True),
     "qwen3_qknorm_hd64": lambda: _mid("qwen3", seed=26, heads=32, kv_heads=8, head_dim=64, qk_norm=True),
+    # head_dim 80 (not a multiple of 32): the attention item's four-warp form
+    "llama_hd80_four_warp_attention": lambda: _mid(seed=28, heads=16, kv_heads=4, head_dim=80, prompt=70),
     "qwen2_ungated_output_bias": _ungated_obias,
 }
 

@@ -4,6 +4,7 @@
 #include "gemv2_impl.cuh"
 
 namespace wgd {
+// row-layout instantiations: gemv_types.cu
 cudaError_t launch_gemv_f32(const GemvArgs &, cudaStream_t, bool, int);
 cudaError_t launch_gemv_f16(const GemvArgs &, cudaStream_t, bool, int);
 cudaError_t launch_gemv_q4_0(const GemvArgs &, cudaStream_t, bool, int);
@@ -11,8 +12,13 @@ cudaError_t launch_gemv_q8_0(const GemvArgs &, cudaStream_t, bool, int);
 cudaError_t launch_gemv_q4_k(const GemvArgs &, cudaStream_t, bool, int);
 cudaError_t launch_gemv_q5_k(const GemvArgs &, cudaStream_t, bool, int);
 cudaError_t launch_gemv_q6_k(const GemvArgs &, cudaStream_t, bool, int);
-cudaError_t launch_gemv2_q4_k(const Gemv2Args &, cudaStream_t, bool, int);
-cudaError_t launch_gemv2_q6_k(const Gemv2Args &, cudaStream_t, bool, int);
+// tensor-core GEMV instantiations for the tiled Q4_K / Q6_K layout (gemv2_impl.cuh)
+cudaError_t launch_gemv2_q4_k(const Gemv2Args &a, cudaStream_t s, bool pdl, int sm_count) {
+  return launch_gemv2_type<Q4_K>(a, s, pdl, sm_count);
+}
+cudaError_t launch_gemv2_q6_k(const Gemv2Args &a, cudaStream_t s, bool pdl, int sm_count) {
+  return launch_gemv2_type<Q6_K>(a, s, pdl, sm_count);
+}
 
 int gemv_max_batch(int cols) {
   if (cols % 32) return 0;

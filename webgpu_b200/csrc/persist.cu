@@ -78,7 +78,6 @@ __device__ __forceinline__ uint64_t gtime() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ void asyncb() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -562,8 +561,8 @@ __device__ __forceinline__ void p_epilogue(GemvCtx &C, int t, float v, int lane)
 
 // ------------------------------------------------------------------ attention item
 
-// One (kv head, key split) of decode attention by consumer warps 0..3 (128
-// threads, named barrier 2); same math and merge order as attention_kernel.
+// One (kv head, key split) of decode attention by consumer warps 0..AW-1 (named barrier 2);
+// same math and merge order as attention_kernel.
 // Shared memory of one attention item (floats): [K|V stage 1][K|V stage 0][q][new k][new v],
 // a stage holding 32 rows of hd + 4 floats each for K and V.
 __device__ __forceinline__ int attn_stage_floats(int hd) { return 2 * 32 * (hd + 4); }
@@ -571,7 +570,8 @@ __device__ __forceinline__ float *attn_stage(float *sm, int hd, int st) { return
 
 // Issue the cp.async copies of K/V rows [tile, min(tile + 32, p1)) of kv head kh into stage st
 // (the row of the position being decoded comes from shared memory instead) and commit them.
-__device__ void p_attn_stage(const PAttn &A, int pos, int kh, int p1, int tile, float *sm, int st, int tid) {
+// Warps 0..nw-1 issue them (tid < 32 * nw).
+__device__ void p_attn_stage(const PAttn &A, int pos, int kh, int p1, int tile, float *sm, int st, int tid, int nw) {
   const int hd = A.hd, RS = hd + 4, end = pos + 1;
   const bool owns_new = p1 == end;
   const float *kb = A.k + (int64_t)kh * A.capacity * hd, *vb = A.v + (int64_t)kh * A.capacity * hd;
@@ -579,7 +579,7 @@ __device__ void p_attn_stage(const PAttn &A, int pos, int kh, int p1, int tile, 
   float *ks = attn_stage(sm, hd, st), *vs = ks + 32 * RS;
   // a warp per key row (the ring slot computed once per row), lanes over its 16-byte pieces
   const int w = tid >> 5, lane = tid & 31;
-  for (int r = w; r < cnt; r += 4) {
+  for (int r = w; r < cnt; r += nw) {
     const int p = tile + r;
     if (owns_new && p == end - 1) continue;
     const int64_t row = (int64_t)(p % A.capacity) * hd;
@@ -599,20 +599,25 @@ __device__ __forceinline__ void attn_split(const PAttn &A, int pos, int nspmax, 
   nsp = (L + chunk - 1) / chunk;
 }
 
-// One (kv head, key split) of decode attention. Every compute warp enters; warps 0..3 (named
-// barrier 2) stage K/V, rotate q/k and run the tiles, and all 14 merge the key splits of the kv head
-// when this CTA is the last to finish one (named barrier 3). Per 32-key tile:
-//   scores   warp w sums dims [w*hd/4, (w+1)*hd/4) for every query head of the group, lane = key
-//            (each K row is read once for all heads), the four parts added in warp order;
-//   softmax  warp w owns heads w, w+4: running max / sum per head (shared memory), the tile's
+// One (kv head, key split) of decode attention. Every compute warp enters; warps 0..AW-1 (named
+// barrier 2; AW = 8 when head_dim is a multiple of 32, else 4) stage K/V, rotate q/k and run the
+// tiles, and all 14 merge the key splits of the kv head when this CTA is the last to finish one (named
+// barrier 3). Per 32-key tile:
+//   scores   warp w sums dims [w*hd/AW, (w+1)*hd/AW) for every query head of the group, lane = key
+//            (each K row is read once for all heads), the AW parts added in warp order;
+//   softmax  warp w owns heads w, w+AW: running max / sum per head (shared memory), the tile's
 //            probabilities to shared memory;
-//   P.V      warp w takes keys j = w (mod 4), lane = four dims, every head at once (each V row read
-//            once), its partial sums rescaled by the heads' corrections; the four warps' sums are
+//   P.V      warp w takes keys j = w (mod AW), lane = four dims, every head at once (each V row read
+//            once), its partial sums rescaled by the heads' corrections; the AW warps' sums are
 //            added in warp order at the end.
 // `staged`: stage 0 already holds the first K/V tile (issued while the QKV projection ran).
-constexpr int AW = 4;  // warps of the tile work
+constexpr int AW_MAX = 8;  // most warps of the tile work (the score scratch is sized for it)
 __device__ __forceinline__ float *attn_scratch(float *sm, int G, int hd) { return sm + 2 * attn_stage_floats(hd) + G * hd + 2 * hd; }
 
+template <int AW>
+__device__ __forceinline__ void abar() { asm volatile("bar.sync 2, %0;" ::"n"(AW * 32) : "memory"); }
+
+template <int AW>
 __device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, int chunk, int nspmax, float *sm, float *att_part,
                             unsigned *att_ctr, int *last_s, bool staged, int tr_step, int tr_phase) {
   (void)tr_step;
@@ -630,8 +635,8 @@ __device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, in
   const int PR = hd + 4;
   float *out_base = A.out + (int64_t)kh * G * hd;
   if (warp < AW) {
-    if (!staged) p_attn_stage(A, pos, kh, p1, p0, sm, 0, tid);
-    if (ntiles > 1) p_attn_stage(A, pos, kh, p1, p0 + 32, sm, 1, tid);
+    if (!staged) p_attn_stage(A, pos, kh, p1, p0, sm, 0, tid, AW);
+    if (ntiles > 1) p_attn_stage(A, pos, kh, p1, p0 + 32, sm, 1, tid, AW);
     const int hq = G + (owns_new ? 1 : 0);
     // this lane's RoPE (cos, sin) pairs, requested together with q/k/v (the same for every head)
     const int half = A.rot / 2;
@@ -650,7 +655,7 @@ __device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, in
       st_s[tid] = -FLT_MAX;
       st_s[8 + tid] = 0.f;
     }
-    asyncb();
+    abar<AW>();
     for (int g = warp; g < hq; g += AW) {
       float *hv = g < G ? q_s + g * hd : kn_s;
       const float *nw = g < G ? A.q_norm : A.k_norm;
@@ -673,26 +678,26 @@ __device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, in
       }
       __syncwarp();
     }
-    asyncb();
+    abar<AW>();
     if (tid == 0) P_TRACE(tr_step, tr_phase, 1);
     if (owns_new) {
       const int slot = pos % A.capacity;
       float *kd = A.k + ((int64_t)kh * A.capacity + slot) * hd, *vd = A.v + ((int64_t)kh * A.capacity + slot) * hd;
       for (int d = tid; d < hd; d += AW * 32) { kd[d] = kn_s[d]; vd[d] = vn_s[d]; }
     }
-    const int dq = hd >> 4;  // float4s of the score dims of one warp
+    const int dq = hd / (4 * AW);  // float4s of the score dims of one warp
     float4 acc[8];
 #pragma unroll
     for (int g = 0; g < 8; g++) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int ti = 0; ti < ntiles; ti++) {
       const int tile = p0 + ti * 32, cnt = min(32, p1 - tile), st = ti & 1;
       if (ti + 1 < ntiles) cp_wait<1>(); else cp_wait<0>();
-      asyncb();
+      abar<AW>();
       float *ks = attn_stage(sm, hd, st), *vs = ks + 32 * RS;
       if (owns_new && tile + cnt == end) {
         const int r = end - 1 - tile;
         for (int d = tid; d < hd; d += AW * 32) { ks[r * RS + d] = kn_s[d]; vs[r * RS + d] = vn_s[d]; }
-        asyncb();
+        abar<AW>();
       }
       {  // scores: this warp's quarter of the dims, every head, lane = key
         const float4 *kr = reinterpret_cast<const float4 *>(ks + lane * RS) + warp * dq;
@@ -714,10 +719,11 @@ __device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, in
         for (int g = 0; g < 8; g++)
           if (g < G) sc_s[(warp * 8 + g) * 32 + lane] = sp2[g][0] + sp2[g][1];
       }
-      asyncb();
+      abar<AW>();
       for (int g = warp; g < G; g += AW) {  // online softmax of head g over this tile
-        float sv = ((sc_s[(0 * 8 + g) * 32 + lane] + sc_s[(1 * 8 + g) * 32 + lane]) + sc_s[(2 * 8 + g) * 32 + lane]) +
-                   sc_s[(3 * 8 + g) * 32 + lane];
+        float sv = sc_s[g * 32 + lane];
+#pragma unroll
+        for (int w = 1; w < AW; w++) sv += sc_s[(w * 8 + g) * 32 + lane];
         const bool live = lane < cnt;
         sv = live ? sv * A.scale : -FLT_MAX;
         const float mo = st_s[g], mn = fmaxf(mo, warp_max(sv)), corr = expf(mo - mn);
@@ -730,8 +736,8 @@ __device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, in
           st_s[16 + g] = corr;
         }
       }
-      asyncb();
-      if (lane < hd4) {  // P.V: keys j = warp (mod 4), four dims per lane, every head
+      abar<AW>();
+      if (lane < hd4) {  // P.V: keys j = warp (mod AW), four dims per lane, every head
         float cr[8];
 #pragma unroll
         for (int g = 0; g < 8; g++) cr[g] = g < G ? st_s[16 + g] : 0.f;
@@ -748,18 +754,18 @@ __device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, in
                                    fmaf(pw[g], v.w, acc[g].w));
         }
       }
-      asyncb();
-      if (ti + 2 < ntiles) p_attn_stage(A, pos, kh, p1, tile + 64, sm, st, tid);
+      abar<AW>();
+      if (ti + 2 < ntiles) p_attn_stage(A, pos, kh, p1, tile + 64, sm, st, tid, AW);
     }
     if (tid == 0) P_TRACE(tr_step, tr_phase, 2);
-    // the four warps' P.V sums, added in warp order (stage 1 is free now: no copy is in flight)
+    // the AW warps' P.V sums, added in warp order (stage 1 is free now: no copy is in flight)
     float4 *cb = reinterpret_cast<float4 *>(sm);  // [AW][G][hd4]
     if (lane < hd4) {
 #pragma unroll
       for (int g = 0; g < 8; g++)
         if (g < G) cb[(warp * G + g) * hd4 + lane] = acc[g];
     }
-    asyncb();
+    abar<AW>();
     for (int i = tid; i < G * hd4; i += AW * 32) {
       const int g = i / hd4, d4 = i - g * hd4;
       float4 t = cb[g * hd4 + d4];
@@ -781,7 +787,7 @@ __device__ void p_attn_item(const PAttn &A, int pos, int kh, int sp, int nsp, in
       }
     }
     if (nsp > 1) __threadfence();
-    asyncb();
+    abar<AW>();
     if (tid == 0 && nsp > 1) *last_s = atomicAdd(att_ctr + kh, 1u) == (unsigned)(nsp - 1);
     if (tid == 0) P_TRACE(tr_step, tr_phase, 4);
   }
@@ -1131,8 +1137,12 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
         const int items = A.kv_heads * nsp;
         if (comp)
           for (int it = c; it < items; it += grid)
-            p_attn_item(A, pos, it / nsp, it % nsp, nsp, chunk, a.nsp_max, reinterpret_cast<float *>(xs), a.att_part, a.att_ctr,
-                        &sh.flags[1], it == c && att_staged, step, p);
+            if (A.hd % 32 == 0)
+              p_attn_item<8>(A, pos, it / nsp, it % nsp, nsp, chunk, a.nsp_max, reinterpret_cast<float *>(xs), a.att_part,
+                             a.att_ctr, &sh.flags[1], it == c && att_staged, step, p);
+            else
+              p_attn_item<4>(A, pos, it / nsp, it % nsp, nsp, chunk, a.nsp_max, reinterpret_cast<float *>(xs), a.att_part,
+                             a.att_ctr, &sh.flags[1], it == c && att_staged, step, p);
         att_staged = false;
         if (tid == 0) P_TRACE(step, p, 3);
         alive = grid_sync(a, gen, stop);
@@ -1172,7 +1182,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) persist_kernel(const PersistArgs
               const int kh = c / nsp, sp = c % nsp;
               const int end = pos + 1, begin = end - (end < A.window ? end : A.window);
               const int p0 = begin + sp * chunk, p1 = min(end, p0 + chunk);
-              p_attn_stage(A, pos, kh, p1, p0, reinterpret_cast<float *>(xs), 0, tid);
+              p_attn_stage(A, pos, kh, p1, p0, reinterpret_cast<float *>(xs), 0, tid, 4);
               att_staged = true;
             }
           }
@@ -1395,8 +1405,8 @@ extern "C" __attribute__((visibility("default"))) int wgd_debug_persist_bars(uin
 // ------------------------------------------------------------------ host side
 
 static int attn_smem_bytes(int group, int hd) {
-  // K|V stages, q, new k and v rows, score parts [4][8][32], probabilities [32][8], head state [3][8]
-  return 4 * (group * hd + 2 * hd + 2 * 2 * 32 * (hd + 4) + 4 * 8 * 32 + 32 * 8 + 3 * 8);
+  // K|V stages, q, new k and v rows, score parts [AW][8][32], probabilities [32][8], head state [3][8]
+  return 4 * (group * hd + 2 * hd + 2 * 2 * 32 * (hd + 4) + AW_MAX * 8 * 32 + 32 * 8 + 3 * 8);
 }
 
 size_t persist_smem_bytes(int max_cols, int group, int hd, int nstage, int *xs, int row_cols) {
