@@ -657,7 +657,7 @@ static int build_persist_plan(wgd_ctx *ctx) {
   if ((rc = ctx_alloc(ctx, (void **)&d_plan, plan.size() * sizeof(PPhase), "decode plan")) ||
       (rc = ctx_alloc_t(ctx, &att_part, (size_t)ctx->kv_l * nsp_max * G * (hd + 4), "decode attention partials")) ||
       (rc = ctx_alloc_t(ctx, &att_ctr, (size_t)ctx->kv_l, "decode attention counters")) ||
-      (rc = ctx_alloc_t(ctx, &cand, (size_t)grid, "decode candidates")) || (rc = ctx_alloc_t(ctx, &bar, 2, "grid barrier")) ||
+      (rc = ctx_alloc_t(ctx, &cand, (size_t)grid, "decode candidates")) || (rc = ctx_alloc_t(ctx, &bar, 4, "grid barrier")) ||
       (rc = ctx_alloc_t(ctx, &status, 4, "decode status")))
     return rc;
 
@@ -704,7 +704,7 @@ static int build_persist_plan(wgd_ctx *ctx) {
 // Per-launch state of the persistent kernel: the grid-barrier counter starts at zero; under tensor
 // parallelism, the peers' exchange buffers and the cross-rank counter base of this launch.
 static int persist_prepare(wgd_ctx *ctx, PersistArgs &a) {
-  CK(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), ctx->stream));  // the arrival counter grows from 0 within a launch
+  CK(cudaMemsetAsync(a.bar, 0, 3 * sizeof(unsigned), ctx->stream));  // the barrier counters grow from 0 within a launch
   if (ctx->tp_size > 1) {
     if (ctx->tp_broken)
       return fail(WGD_ETIMEOUT, "a tensor-parallel peer did not answer within the wait limit earlier; reload the model");
@@ -728,7 +728,7 @@ static void persist_account(wgd_ctx *ctx) {
   if (ctx->tp_size < 2) return;
   const unsigned done = (unsigned)ctx->h_io[IO_STATUS + 1];
   if (ctx->h_io[IO_STATUS] == 1) ctx->tp_broken = true;
-  ctx->x_arrivals += done * (2u * (unsigned)ctx->c.layers + 1u) * (unsigned)(ctx->tp_size * ctx->sm_count);
+  ctx->x_arrivals += done * (2u * (unsigned)ctx->c.layers + 1u) * (unsigned)ctx->tp_size;
   ctx->x_tokens += done;
 }
 

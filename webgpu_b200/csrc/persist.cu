@@ -907,28 +907,55 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, unsigned par, volatile in
 }
 
 // Barrier over every CTA of every rank of a tensor-parallel group, after this CTA's partial rows
-// were pushed to the peers: each CTA adds 1 to the arrival counter in every rank's exchange
-// buffer (system-scope release, after a system-scope fence), then polls its own rank's counter
-// until all tp * grid arrivals of this barrier are in. The counter only grows (across launches
-// too: xbase is the count before this launch), so no reset races a faster peer.
+// were pushed to the peers. Two levels: every CTA makes its peer stores visible (system-scope
+// fence) and arrives on its rank's local counter (bar[1]); CTA 0 waits for the rank's CTAs, adds 1
+// to the arrival counter in every rank's exchange buffer (one system-scope release per rank instead
+// of one per CTA), waits until its own rank's counter holds every rank's arrival, and releases the
+// rank's CTAs through a local generation word (bar[2]). The counters only grow (the exchange
+// counter across launches too: xbase is its count before this launch), so no reset races a faster
+// peer. A wait that runs out (x_limit_ns) raises the status; CTA 0 releases its rank's CTAs also then.
 __device__ bool x_sync(const PersistArgs &a, unsigned &xgen, volatile int *stop) {
   bar_all();
   if (threadIdx.x == 0 && !*stop) {
     __threadfence_system();
-    for (int j = 0; j < a.tp; j++)
-      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.xbuf[j] + a.x_bar) : "memory");
-    const unsigned target = a.xbase + (xgen + 1u) * (unsigned)(gridDim.x * a.tp);
-    const unsigned *ctr = reinterpret_cast<const unsigned *>(a.xbuf[a.rank] + a.x_bar);
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar + 1) : "memory");
     const uint64_t t0 = gtime();
-    for (unsigned it = 1;; it++) {
-      unsigned v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
-      if ((int)(v - target) >= 0) break;
-      if ((it & 63) == 0 && (*(volatile int *)a.status == 1 || gtime() - t0 > a.x_limit_ns)) {
+    if (blockIdx.x == 0) {
+      bool ok = true;
+      const unsigned lt = (xgen + 1u) * gridDim.x;
+      for (unsigned it = 1; (int)(ld_acquire(a.bar + 1) - lt) < 0; it++)
+        if ((it & 63) == 0 && (*(volatile int *)a.status == 1 || gtime() - t0 > a.x_limit_ns)) {
+          ok = false;
+          break;
+        }
+      if (ok) {
+        __threadfence_system();
+        for (int j = 0; j < a.tp; j++)
+          asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.xbuf[j] + a.x_bar) : "memory");
+        const unsigned target = a.xbase + (xgen + 1u) * (unsigned)a.tp;
+        const unsigned *ctr = reinterpret_cast<const unsigned *>(a.xbuf[a.rank] + a.x_bar);
+        for (unsigned it = 1;; it++) {
+          unsigned v;
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+          if ((int)(v - target) >= 0) break;
+          if ((it & 63) == 0 && (*(volatile int *)a.status == 1 || gtime() - t0 > a.x_limit_ns)) {
+            ok = false;
+            break;
+          }
+        }
+      }
+      if (!ok) {
         atomicCAS(a.status, 0, 1);
         *stop = 1;
-        break;
       }
+      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.bar + 2), "r"(xgen + 1u) : "memory");
+    } else {
+      for (unsigned it = 1; (int)(ld_acquire(a.bar + 2) - (xgen + 1u)) < 0; it++)
+        if ((it & 63) == 0 && gtime() - t0 > a.x_limit_ns + P_TIMEOUT_NS) {
+          atomicCAS(a.status, 0, 1);
+          break;
+        }
+      if (*(volatile int *)a.status == 1) *stop = 1;
     }
     xgen++;
   }

@@ -73,7 +73,8 @@ struct PersistArgs {
   float *att_part;      // [kv_heads][nsp_max][group][hd + 4]
   unsigned *att_ctr;    // [kv_heads] (zero, left zero)
   float2 *cand;         // [grid] (best logit, index bits) of each CTA
-  unsigned *bar;        // grid barrier: [0] arrivals, zero at launch and growing by grid per barrier
+  unsigned *bar;        // [0] grid-barrier arrivals, [1] cross-rank barrier arrivals of this rank's CTAs,
+                        // [2] cross-rank barrier generations released to this rank's CTAs; zero at launch
   int *status;          // [0] 0 ok, 1 wait limit hit, 2 non-finite logits, 3 cancelled; [1] steps done
   int nstage, xs_bytes, nsp_max;
   int l2_ahead;  // ring stages requested into L2 ahead of the shared-memory copies (0: none)
@@ -81,7 +82,7 @@ struct PersistArgs {
   int tp, rank, vocab0;
   char *xbuf[P_TP_MAX];
   unsigned long long x_bar, x_cand, x_slot;  // byte offsets of the kernel's region in an exchange buffer
-  unsigned xbase;   // arrivals counted on this rank's cross-rank counter before this launch
+  unsigned xbase;   // arrivals counted on this rank's cross-rank counter before this launch (one per rank and barrier)
   unsigned xstep0;  // tokens decoded by earlier launches of this group (candidate slot parity)
   unsigned long long x_limit_ns;  // bound of one cross-rank wait
 };
