@@ -20,7 +20,10 @@
 //    a tile's chunks in k-block order, so every sum has a fixed order. A result
 //    stage is free again without a barrier of its own: stage g + ns of the
 //    weight ring is only issued after the epilogue warp has read the results of
-//    stage g, and ns <= P_RES_STAGES.
+//    stage g, and ns <= P_RES_STAGES;
+//  * tensor parallel, after a phase whose outputs are pushed to the peers (O,
+//    down) and after the LM head, a two-level cross-rank barrier (x_sync)
+//    replaces the grid barrier.
 // Every wait is bounded by a globaltimer deadline; a wait that runs out sets
 // status[0] = 1 and the whole grid winds down (the producer first waits for its
 // copies in flight).
